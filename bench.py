@@ -1,0 +1,383 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 D64 BF16 FMHA forward (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl native|reference]
+
+One step = one forward pass over the workload.  Default workload is
+BASELINE configs[1] (B4 H16 S2048 non-causal).  Multi-GPU (torchrun, one rank
+per GPU): every rank runs its own shard of a global batch that grows with N
+(weak scaling, no collective on the data path); time = max over ranks.
+
+`--impl reference` times the reference's own CPU implementation of the path
+(its cpu_ref_verify, compiled from its sources into oracle/_ref) on a bounded
+sample of the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "d64 bf16 FMHA fwd TFLOP/s per B200 (causal ×0.5), % of BF16 tensor peak"
+UNIT = "TFLOP/s"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n_, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n_)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def reference_arm(args, workload_key):
+    """CPU baseline: the reference's cpu_ref_verify on a bounded sample."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    from fmha_native_b200.synth import WORKLOADS
+
+    w = WORKLOADS[workload_key]
+    if not O.have_reference():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref/libfmha_ref.so not built (reference tree absent at build)"}))
+        return 0
+    sample = cpu_sample(w)
+    res = time_cpu_reference(O, sample, args.steps, args.warmup)
+    line = {
+        "metric": METRIC, "value": res["tflops"], "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 in / fp32 accumulate (CPU)", "data": "synthetic",
+        "config": {"workload": w.name, "sample": sample["desc"]},
+        "cpu_baseline": {"value": res["tflops"], "unit": UNIT, "cores": res["threads"],
+                         "kind": "reference", "sample": sample["desc"]},
+        "e2e": {"value": res["tflops"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def cpu_sample(w):
+    """A bounded sample of workload `w` for the reference CPU oracle: every
+    (batch, head) pair, a slice of the query rows, all keys they attend.
+    For non-causal rows the per-row cost is the full workload's, so FLOPs
+    scale exactly; causal samples use the last query rows (full-length
+    rows, the worst case) and count their exact unmasked area."""
+    if w.varlen_seqs:
+        seqs = list(w.varlen_seqs)[:4]
+        b, h, s = len(seqs), w.heads, max(seqs)
+        sq = 256
+        return {"desc": f"varlen first 4 seqs {seqs}, H{h}, 256 query rows each (as Sq=256, Sk=S_b)",
+                "b": 1, "h": h, "sq": sq, "sk": seqs[0], "causal": w.causal,
+                "flops": 4.0 * h * sq * seqs[0] * 64 * (1.0 if not w.causal else (1 - (sq - 1) / (2.0 * seqs[0])))}
+    b, h, s = w.batch, w.heads, w.seqlen
+    sq = 256 if s >= 256 else s
+    if b * h < 4:
+        sq = min(s, 128)
+    flops = 4.0 * b * h * sq * s * 64
+    if w.causal:
+        # rows i = S-sq..S-1 attend i+1 keys
+        keys = sum(range(s - sq + 1, s + 1))
+        flops = 4.0 * b * h * keys * 64
+    return {"desc": f"B{b} H{h}: last {sq} query rows x {s} keys ({'causal' if w.causal else 'non-causal'})",
+            "b": b, "h": h, "sq": sq, "sk": s, "causal": w.causal, "flops": flops}
+
+
+def time_cpu_reference(O, sample, steps, warmup):
+    import numpy as np
+
+    b, h, sq, sk = sample["b"], sample["h"], sample["sq"], sample["sk"]
+    rng = np.random.default_rng(0)
+    q = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sq * 64).astype(np.float32))
+    k = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sk * 64).astype(np.float32))
+    v = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sk * 64).astype(np.float32))
+    o = np.zeros(b * h * sq * 64, np.uint16)
+    times = []
+    for it in range(warmup + steps):
+        t0 = time.perf_counter()
+        O.ref_verify(b, h, h, sq, sk, int(sample["causal"]), [], q, k, v, o)
+        dt = time.perf_counter() - t0
+        if it >= warmup:
+            times.append(dt)
+    ms = 1000.0 * sum(times) / len(times)
+    # cpu_ref_verify parallelises (b,h) pairs in chunks of 16 (cpu_ref.cpp:84)
+    threads = min(os.cpu_count() or 1, max(1, -(-(b * h) // 16)))
+    return {"ms": ms, "tflops": sample["flops"] / (ms * 1e-3) / 1e12, "threads": threads}
+
+
+def native_arm(args, workload_key):
+    import torch
+
+    import fmha_native_b200 as fm
+    from fmha_native_b200.synth import WORKLOADS, make_inputs
+
+    rank, world, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    fm.load_library()
+    w = WORKLOADS[workload_key]
+    q, k, v, cu = make_inputs(w, dev, seed_base=1000 * rank)
+    layout = w.layout
+    o = torch.empty_like(q)
+    lse = None
+    if w.lse:
+        if w.varlen_seqs:
+            lse = torch.empty(w.heads, w.tokens(), device=dev, dtype=torch.float32)
+        else:
+            lse = torch.empty(w.batch, w.heads, w.seqlen, device=dev, dtype=torch.float32)
+    params, batch, tq, tk = fm.params_from_tensors(q, k, v, o, lse, layout, cu, cu)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
+
+    def step():
+        st = fm.call_entry(params, batch, w.causal, bool(w.varlen_seqs), tq, tk, sh)
+        if st != fm.FMHA_OK:
+            raise fm.FmhaError(st, "launch")
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if fm.status(sh) != fm.FMHA_OK:
+        raise RuntimeError("device pipeline timeout during warmup")
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()  # L2 flush between timed launches (outside the events)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop()
+    kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(kern_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    if fm.status(sh) != fm.FMHA_OK:
+        raise RuntimeError("device pipeline timeout during timed steps")
+    ms_step = total_ms / args.steps
+    flops_rank = w.flops()
+    value = world * flops_rank / (ms_step * 1e-3) / 1e12
+    peak_tf, peak_hbm, peak_kind = load_peaks()
+    achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
+
+    # ---- e2e: host buffers through the public API, copies inside the timed region
+    e2e = e2e_measure(fm, w, dev, args, params_builder=(layout, cu))
+    if world > 1:
+        t = torch.tensor([e2e["ms"]], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e["ms"] = float(t.item())
+    e2e_value = world * flops_rank / (e2e["ms"] * 1e-3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w)
+
+    if rank == 0:
+        alg_bytes = 2 * (q.numel() + k.numel() + v.numel() + o.numel()) + (
+            lse.numel() * 4 if lse is not None else 0)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w.name, "per_gpu_batch": w.batch, "global_batch": w.batch * world,
+                       "heads": w.heads, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
+                       "lse": w.lse, "parallelism": f"shard by (batch, head) over {world} GPU(s), "
+                       "K/V local, no collective", "l2": "flushed (256 MiB write) between steps"},
+            "pct_of_bf16_peak": round(100.0 * (value / world) / peak_tf, 2),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_tf,
+                         "unit": UNIT, "frac": round(achieved / peak_tf, 4),
+                         "peak_kind": f"{peak_kind} bf16_tflops (burst)",
+                         "alg_bytes_per_launch": alg_bytes, "traffic": args.traffic},
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT,
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "ms_per_step": round(e2e["ms"], 4)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def e2e_measure(fm, w, dev, args, params_builder):
+    """Public API with pinned host buffers: H2D of Q,K,V (and cu_seqlens),
+    the kernel, D2H of O (and LSE) -- all inside CUDA events."""
+    import torch
+    from fmha_native_b200.synth import make_inputs
+
+    q, k, v, cu = make_inputs(w, dev, seed_base=77)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hcu = cu.cpu().pin_memory() if cu is not None else None
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dcu = torch.empty_like(cu) if cu is not None else None
+    hl = None
+    stream = torch.cuda.current_stream(dev)
+    h2d = 3 * hq.numel() * 2 + (hcu.numel() * 4 if hcu is not None else 0)
+    d2h = ho.numel() * 2
+
+    def one():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        if dcu is not None:
+            dcu.copy_(hcu, non_blocking=True)
+        o = fm.fmha_fwd(dq, dk, dv, causal=w.causal, return_lse=False, layout=w.layout,
+                        cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream)
+        ho.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 10))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(n):
+        one()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return {"ms": s.elapsed_time(e) / n, "h2d": h2d, "d2h": d2h}
+
+
+def cpu_baseline(w):
+    try:
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+
+        sample = cpu_sample(w)
+        if O.have_reference():
+            res = time_cpu_reference(O, sample, steps=2, warmup=0)
+            kind = "reference"
+        else:
+            return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                    "sample": "unavailable: oracle/_ref not built"}
+        return {"value": round(res["tflops"], 6), "unit": UNIT, "cores": res["threads"],
+                "kind": kind, "sample": sample["desc"], "ms_per_sample": round(res["ms"], 1),
+                "host_cpus": os.cpu_count()}
+    except Exception as exc:  # reported, never fatal to the GPU number
+        return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
+                "sample": f"failed: {exc}"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per launch to report in roofline.traffic")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args, args.config)
+    return native_arm(args, args.config)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,65 @@
+"""In-tree build of the sm_100a CUDA library (``libfmha_b200.so``).
+
+The library is compiled with nvcc directly (no JIT cache) so the built
+``.so`` sits next to this file and travels with the source tree.  Usage::
+
+    python -m fmha_native_b200.build          # build if sources are newer
+    python -m fmha_native_b200.build --force  # always rebuild
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+LIB_PATH = os.path.join(PKG_DIR, "libfmha_b200.so")
+
+SOURCES = [os.path.join(CSRC, "fmha_fwd_kernel.cu")]
+DEPS = SOURCES + [
+    os.path.join(CSRC, "sm100_ptx.cuh"),
+    os.path.join(REPO_DIR, "include", "fmha_fwd.h"),
+]
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _stale(target: str, deps: list[str]) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build_library(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> str:
+    """Compile ``libfmha_b200.so`` for sm_100a; returns its path."""
+    if not force and not extra_flags and not _stale(LIB_PATH, DEPS):
+        return LIB_PATH
+    cmd = [
+        nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+        "-Xcompiler", "-fPIC", "-shared", "--cudart", "static",
+        "-I", os.path.join(REPO_DIR, "include"),
+        *(extra_flags or []),
+        *SOURCES, "-o", LIB_PATH + ".tmp",
+    ]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(LIB_PATH + ".tmp", LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    build_library(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(LIB_PATH)

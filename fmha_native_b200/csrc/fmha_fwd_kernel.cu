@@ -1,0 +1,794 @@
+// fmha_fwd_kernel.cu -- B200 (sm_100a) head-dim-64 BF16 fused attention
+// forward, and the C-ABI launchers declared in include/fmha_fwd.h.
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and walks the
+// key/value sequence in 128-key tiles.  It is warp specialised:
+//
+//   warps 0-3  softmax group 0  : rows of query tile 0 (one row per thread)
+//   warps 4-7  softmax group 1  : rows of query tile 1
+//   warp  8    TMA producer     : Q tiles once, then K_j / V_j into a ring
+//   warp  9    MMA issuer       : one thread issues every tcgen05.mma; the
+//                                 warp also owns the TMEM allocation
+//
+// Tensor memory (512 columns x 128 lanes, fp32):
+//   [  0,128) S0 = Q0 K^T   (its first 64 columns are reused for P0 as bf16x2)
+//   [128,256) S1 = Q1 K^T   (P1 likewise)
+//   [256,320) O0 accumulator
+//   [320,384) O1 accumulator
+//
+// Per KV tile j and query tile i the schedule is
+//   MMA : S_i = Q_i K_j^T  -> commit(s_full[i])
+//   SM_i: S -> row max -> (lazy) rescale O_i -> P = exp2(S*scale - m*scale)
+//         -> bf16 P into TMEM -> arrive(p_full[i])
+//   MMA : O_i += P_i V_j, then S_i = Q_i K_{j+1}^T immediately
+// so the two softmax groups run half a period apart and the tensor core
+// alternates between them.  tcgen05 MMAs issued by one thread execute in
+// order, so S_i(j+1) overwriting P_i(j) is safe once O_i += P_i V_j is issued,
+// and s_full[i] (committed after S_i(j+1)) also proves O_i += P_i V_j is
+// complete, which is what makes the softmax-side O rescale race free.
+//
+// Reference semantics followed (poyenc/fmha_native):
+//   grid decode + causal heavy-first order ... src/fused/kernel.cpp:55-99
+//   varlen offsets, causal KV end ........... src/fused/pipeline.hpp:116-193
+//   degenerate tile (no key) -> O=0, LSE=-inf src/fused/pipeline.hpp:207-222
+//   boundary / causal masking ............... src/fused/op_softmax.hpp:73-131
+//   exp2 softmax with log2e-folded scale .... src/fused/op_softmax.hpp:148-255
+//   P truncated to bf16 before P.V .......... src/fused/op_gemm.hpp:272-273
+//   O * (1/l), bf16 truncation, LSE ......... src/fused/op_epilog.hpp:50-155
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/fmha_fwd.h"
+#include "sm100_ptx.cuh"
+
+using namespace fmha_sm100;
+
+namespace {
+
+constexpr int kBlockM = 128;            // rows per query tile
+constexpr int kBlockN = 128;            // keys per KV tile
+constexpr int kHeadDim = 64;
+constexpr int kTilesPerCta = 2;         // query tiles per CTA
+constexpr int kRowsPerCta = kBlockM * kTilesPerCta;
+constexpr int kStages = 6;              // K/V ring slots (K_j, V_j alternate)
+constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
+constexpr int kThreads = 320;
+constexpr int kWarpLoad = 8;
+constexpr int kWarpMma = 9;
+constexpr uint32_t kTmemCols = 512;
+__host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i / P_i
+__host__ __device__ constexpr uint32_t col_o(int i) { return 256u + i * 64u; }  // O_i
+// Lazy rescale threshold in log2 units: the running max is only moved when
+// it grows by more than this, bounding un-normalised P by 2^8.
+constexpr float kRescaleThreshold = 8.0f;
+
+// Error codes written to the device error word.
+constexpr int kErrTimeoutLoad = 0x101;
+constexpr int kErrTimeoutMma = 0x102;
+constexpr int kErrTimeoutSoftmax = 0x103;
+
+struct KernelArgs {
+    CUtensorMap tm_q;
+    CUtensorMap tm_k;
+    CUtensorMap tm_v;
+    uint16_t* o;
+    float* lse;
+    const int32_t* seqstart_q;
+    const int32_t* seqstart_k;
+    long long stride_o, nhead_stride_o, batch_stride_o;
+    int seqlen_q, seqlen_k;
+    int nhead_q, nhead_k;
+    int total_q;               // varlen: LSE head stride
+    float scale;
+    int* err_word;
+    unsigned long long wait_limit_ns;
+    int stall_inject;          // test hook: producer withholds the first V tile
+};
+
+struct alignas(1024) SharedStorage {
+    uint8_t q[kTilesPerCta][kTileBytes];
+    uint8_t kv[kStages][kTileBytes];
+    uint64_t bar_q[kTilesPerCta];
+    uint64_t bar_full[kStages];
+    uint64_t bar_empty[kStages];
+    uint64_t bar_s[kTilesPerCta];
+    uint64_t bar_p[kTilesPerCta];
+    uint64_t bar_o[kTilesPerCta];
+    uint64_t bar_drain;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+// Bounded wait on an mbarrier phase.  Returns false if the CTA-wide abort
+// flag is raised or the time limit expires (then it raises the flag and
+// records `code` in the device error word).
+__device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                        const KernelArgs& a, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > a.wait_limit_ns) {
+                *abort_flag = 1;
+                atomicCAS(a.err_word, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait used only while tearing down after an abort: ignores the
+// abort flag, gives up silently after the time limit.
+__device__ __noinline__ void drain_phase(uint32_t bar, uint32_t parity, const KernelArgs& a) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > a.wait_limit_ns) return;
+    }
+}
+
+struct TileWork {
+    int n_kv[kTilesPerCta];     // KV tiles each query tile walks
+    int row0;                   // first query row of the CTA (sequence-local)
+    int seqlen_q, seqlen_k;
+    int off_q, off_k;           // varlen packed-row offsets
+    int b, h, kvh;
+};
+
+template <bool kCausal, bool kVarlen>
+__device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
+    const int hb = blockIdx.x;
+    w.h = hb % a.nhead_q;
+    w.b = hb / a.nhead_q;
+    w.kvh = w.h / (a.nhead_q / a.nhead_k);
+    // Causal work grows with the query block index, so launch the heavy
+    // blocks first (src/fused/kernel.cpp:73,96).
+    const int mblk = kCausal ? (int)(gridDim.y - 1 - blockIdx.y) : (int)blockIdx.y;
+    if constexpr (kVarlen) {
+        w.off_q = a.seqstart_q[w.b];
+        w.off_k = a.seqstart_k[w.b];
+        w.seqlen_q = a.seqstart_q[w.b + 1] - w.off_q;
+        w.seqlen_k = a.seqstart_k[w.b + 1] - w.off_k;
+    } else {
+        w.off_q = 0;
+        w.off_k = 0;
+        w.seqlen_q = a.seqlen_q;
+        w.seqlen_k = a.seqlen_k;
+    }
+    w.row0 = mblk * kRowsPerCta;
+    if (w.row0 >= w.seqlen_q) return false;
+    const int shift = w.seqlen_k - w.seqlen_q;  // bottom-right causal alignment
+#pragma unroll
+    for (int i = 0; i < kTilesPerCta; ++i) {
+        const int r0 = w.row0 + i * kBlockM;
+        if (r0 >= w.seqlen_q) {
+            w.n_kv[i] = 0;
+            continue;
+        }
+        int kv_end = w.seqlen_k;
+        if (kCausal) {
+            const int r_last = min(r0 + kBlockM - 1, w.seqlen_q - 1);
+            kv_end = min(w.seqlen_k, r_last + shift + 1);
+        }
+        w.n_kv[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+    }
+    return true;
+}
+
+template <bool kVarlen>
+__device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* tm, uint32_t bar,
+                                              int row, int head, int batch, uint64_t policy) {
+    if constexpr (kVarlen) {
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+            " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+            ::"r"(dst), "l"(tm), "r"(0), "r"(row), "r"(head), "r"(bar), "l"(policy)
+            : "memory");
+    } else {
+        tma_load_4d(dst, tm, bar, 0, row, head, batch, policy);
+    }
+}
+
+template <bool kCausal, bool kVarlen>
+__global__ void __launch_bounds__(kThreads, 1)
+fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    SharedStorage& sm = *reinterpret_cast<SharedStorage*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+    TileWork w;
+    if (!decode_work<kCausal, kVarlen>(a, w)) return;  // CTA-uniform early out
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    volatile int* abort_flag = &sm.abort_flag;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kTilesPerCta; ++i) {
+            mbar_init(smem_u32(&sm.bar_q[i]), 1);
+            mbar_init(smem_u32(&sm.bar_s[i]), 1);
+            mbar_init(smem_u32(&sm.bar_p[i]), kBlockM);
+            mbar_init(smem_u32(&sm.bar_o[i]), 1);
+        }
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&sm.bar_full[s]), 1);
+            mbar_init(smem_u32(&sm.bar_empty[s]), 1);
+        }
+        mbar_init(smem_u32(&sm.bar_drain), 1);
+        sm.abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == kWarpMma) {
+        tmem_alloc(smem_u32(&sm.tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sm.tmem_base;
+
+    const int n_max = max(w.n_kv[0], w.n_kv[1]);
+
+    if (warp == kWarpLoad) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&a.tm_q);
+            tma_prefetch_desc(&a.tm_k);
+            tma_prefetch_desc(&a.tm_v);
+            const uint64_t pol_q = l2_policy_evict_first();
+            const uint64_t pol_kv = l2_policy_evict_last();
+            const int qbatch = kVarlen ? 0 : w.b;
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (w.n_kv[i] == 0) continue;
+                const uint32_t bar = smem_u32(&sm.bar_q[i]);
+                mbar_arrive_expect_tx(bar, kTileBytes);
+                tma_load_rows<kVarlen>(smem_u32(sm.q[i]), &a.tm_q, bar,
+                                       w.off_q + w.row0 + i * kBlockM, w.h, qbatch, pol_q);
+            }
+            int issued = 0;  // loads issued into the ring
+            bool ok = true;
+            const int n_loads = 2 * n_max;
+            for (int idx = 0; idx < n_loads; ++idx) {
+                const int slot = idx % kStages;
+                const uint32_t use = idx / kStages;
+                if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag, a,
+                                kErrTimeoutLoad)) {
+                    ok = false;
+                    break;
+                }
+                if (a.stall_inject && idx == 1) {
+                    // Test hook: never deliver V_0, so the MMA warp's wait runs
+                    // out and the abort path is exercised without any fault.
+                    continue;
+                }
+                const uint32_t bar = smem_u32(&sm.bar_full[slot]);
+                mbar_arrive_expect_tx(bar, kTileBytes);
+                const CUtensorMap* tm = (idx & 1) ? &a.tm_v : &a.tm_k;
+                tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), tm, bar,
+                                       w.off_k + (idx >> 1) * kBlockN, w.kvh,
+                                       kVarlen ? 0 : w.b, pol_kv);
+                issued = idx + 1;
+            }
+            if (!ok || *abort_flag) {
+                // Let every copy this warp started land before the CTA exits.
+                for (int i = 0; i < kTilesPerCta; ++i)
+                    if (w.n_kv[i] > 0) drain_phase(smem_u32(&sm.bar_q[i]), 0, a);
+                for (int idx = max(0, issued - kStages); idx < issued; ++idx) {
+                    if (a.stall_inject && idx == 1) continue;
+                    drain_phase(smem_u32(&sm.bar_full[idx % kStages]), (idx / kStages) & 1, a);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == kWarpMma) {
+        // ------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_qk = idesc_bf16_f32(kBlockM, kBlockN, 0, 0);
+            constexpr uint32_t idesc_pv = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
+            const uint32_t q_base[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
+            const uint32_t kv_base = smem_u32(sm.kv[0]);
+            bool ok = true;
+
+            auto slot_of = [](int idx) { return idx % kStages; };
+            auto full_parity = [](int idx) { return (uint32_t)((idx / kStages) & 1); };
+
+            // S_i = Q_i K^T : M=128, N=128, K=64 as 4 x K16 (32 bytes apart
+            // inside the 128-byte swizzled rows).
+            auto issue_s = [&](int i, int slot) {
+                const uint32_t kaddr = kv_base + slot * kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+                    const uint64_t da = smem_desc_sw128(q_base[i] + kk * 32, 16, 1024);
+                    const uint64_t db = smem_desc_sw128(kaddr + kk * 32, 16, 1024);
+                    mma_ss(tmem + col_s(i), da, db, idesc_qk, kk > 0);
+                }
+            };
+            // O_i += P_i V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the
+            // TMEM A operand; V is MN-major in shared memory, 16 keys = two
+            // 8-row swizzle atoms = 2048 bytes per step.
+            auto issue_pv = [&](int i, int slot, bool accumulate) {
+                const uint32_t vaddr = kv_base + slot * kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < kBlockN / 16; ++kk) {
+                    const uint64_t db = smem_desc_sw128(vaddr + kk * 2048, 0, 1024);
+                    mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, db, idesc_pv,
+                           (accumulate || kk > 0) ? 1u : 0u);
+                }
+            };
+
+            for (int i = 0; i < kTilesPerCta && ok; ++i)
+                if (w.n_kv[i] > 0)
+                    ok = wait_phase(smem_u32(&sm.bar_q[i]), 0, abort_flag, a, kErrTimeoutMma);
+            if (ok && n_max > 0) {
+                ok = wait_phase(smem_u32(&sm.bar_full[slot_of(0)]), full_parity(0), abort_flag, a,
+                                kErrTimeoutMma);
+                if (ok) {
+                    tc_fence_after();
+                    for (int i = 0; i < kTilesPerCta; ++i) {
+                        if (w.n_kv[i] == 0) continue;
+                        issue_s(i, slot_of(0));
+                        mma_commit(smem_u32(&sm.bar_s[i]));
+                    }
+                    mma_commit(smem_u32(&sm.bar_empty[slot_of(0)]));
+                }
+            }
+            for (int j = 0; j < n_max && ok; ++j) {
+                const int v_idx = 2 * j + 1;
+                const int k_idx = 2 * j + 2;
+                ok = wait_phase(smem_u32(&sm.bar_full[slot_of(v_idx)]), full_parity(v_idx),
+                                abort_flag, a, kErrTimeoutMma);
+                if (!ok) break;
+                tc_fence_after();
+                bool k_ready = false;
+                for (int i = 0; i < kTilesPerCta; ++i) {
+                    if (j >= w.n_kv[i]) continue;
+                    ok = wait_phase(smem_u32(&sm.bar_p[i]), j & 1, abort_flag, a, kErrTimeoutMma);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(i, slot_of(v_idx), j > 0);
+                    if (j == w.n_kv[i] - 1) mma_commit(smem_u32(&sm.bar_o[i]));
+                    if (j + 1 < w.n_kv[i]) {
+                        if (!k_ready) {
+                            ok = wait_phase(smem_u32(&sm.bar_full[slot_of(k_idx)]),
+                                            full_parity(k_idx), abort_flag, a, kErrTimeoutMma);
+                            if (!ok) break;
+                            tc_fence_after();
+                            k_ready = true;
+                        }
+                        issue_s(i, slot_of(k_idx));
+                        mma_commit(smem_u32(&sm.bar_s[i]));
+                    }
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(&sm.bar_empty[slot_of(v_idx)]));
+                if (k_ready) mma_commit(smem_u32(&sm.bar_empty[slot_of(k_idx)]));
+            }
+            // All MMAs this thread issued must finish before TMEM is freed.
+            mma_commit(smem_u32(&sm.bar_drain));
+            drain_phase(smem_u32(&sm.bar_drain), 0, a);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------ softmax groups
+        const int i = warp >> 2;                    // query tile of this group
+        const int t = threadIdx.x & (kBlockM - 1);  // row inside the tile == TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lane_base + col_s(i);
+        const uint32_t tO = tmem + lane_base + col_o(i);
+        const int n = w.n_kv[i];
+        const int tile_row0 = w.row0 + i * kBlockM;
+        const int row = tile_row0 + t;
+        const int shift = w.seqlen_k - w.seqlen_q;
+        const float scale = a.scale;
+        // Keys visible to this row: [0, key_lim).
+        const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
+
+        float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
+        float l_run = 0.0f;       // running sum of un-normalised P
+        bool ok = true;
+
+        for (int j = 0; j < n; ++j) {
+            bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t r[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) reg_fence(r[c]);
+
+            const int k0 = j * kBlockN;
+            const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
+                                   (kCausal && k0 + kBlockN - 1 > tile_row0 + shift);
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
+            }
+            float mx[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int q = c * 2 + (e >> 4);
+                    if ((e & 15) != 0) mx[q] = fmaxf(mx[q], __uint_as_float(r[c][e]));
+                }
+            const float row_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+            const float m_new = fmaxf(m_run, row_max);
+            const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
+            float alpha = 1.0f;
+            if (upd) {
+                alpha = ex2_approx((m_run - m_new) * scale);
+                m_run = m_new;
+            }
+            l_run *= alpha;
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            const float neg_ms = -m_use * scale;
+            float sum[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) sum[q] = 0.0f;
+            uint32_t p[2][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][e]), scale, neg_ms));
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][e + 1]), scale, neg_ms));
+                    const int q = (c * 2 + (e >> 4));
+                    sum[q] += p0 + p1;
+                    p[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16_trunc(p0, p1);
+                }
+            l_run += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
+            tmem_st32(tS, p[0]);
+            tmem_st32(tS + 32, p[1]);
+            if (j > 0 && __any_sync(0xffffffffu, upd)) {
+                // O_i is quiescent here: s_full for S_i(j) was committed after
+                // O_i += P_i(j-1) V_{j-1}, and O_i += P_i(j) V_j waits for p_full.
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+                    reg_fence(o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sm.bar_p[i]));
+        }
+
+        // ---------------------------------------------------- epilogue
+        if (ok && n > 0) {
+            bool got = wait_phase(smem_u32(&sm.bar_o[i]), 0, abort_flag, a, kErrTimeoutSoftmax);
+            ok = __all_sync(0xffffffffu, got);
+        }
+        if (ok) {
+            uint32_t o[2][32];
+            if (n > 0) {
+                tc_fence_after();
+                tmem_ld32(tO, o[0]);
+                tmem_ld32(tO + 32, o[1]);
+                tmem_wait_ld();
+                reg_fence(o[0]);
+                reg_fence(o[1]);
+            }
+            if (row < w.seqlen_q) {
+                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+                uint16_t* orow;
+                if constexpr (kVarlen) {
+                    orow = a.o + (long long)w.h * a.nhead_stride_o +
+                           (long long)(w.off_q + row) * a.stride_o;
+                } else {
+                    orow = a.o + (long long)w.b * a.batch_stride_o +
+                           (long long)w.h * a.nhead_stride_o + (long long)row * a.stride_o;
+                }
+                uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = c * 8 + e * 2;
+                        const float v0 = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
+                        const float v1 = n > 0 ? __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l : 0.0f;
+#ifdef FMHA_O_ROUND_RNE
+                        pk[e] = pack_bf16_rne(v0, v1);
+#else
+                        pk[e] = pack_bf16_trunc(v0, v1);
+#endif
+                    }
+                    dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+                if (a.lse != nullptr) {
+                    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                    const float lse = (l_run > 0.0f)
+                                          ? (__log2f(l_run) + m_use * scale) * 0.69314718055994531f
+                                          : -INFINITY;
+                    long long idx;
+                    if constexpr (kVarlen) {
+                        idx = (long long)w.h * a.total_q + w.off_q + row;
+                    } else {
+                        idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
+                    }
+                    a.lse[idx] = lse;
+                }
+            }
+        }
+    }
+
+    // ---------------------------------------------------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ====================================================================== host
+
+struct DeviceContext {
+    bool ready = false;
+    int* err_word = nullptr;
+};
+
+std::mutex g_mutex;
+std::vector<DeviceContext> g_devices;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+unsigned long long g_wait_limit_ns = 2000000000ull;
+int g_stall_inject = 0;
+
+template <bool C, bool V>
+constexpr size_t kernel_smem_bytes() {
+    return sizeof(SharedStorage) + 1024;
+}
+
+int ensure_context(int dev, DeviceContext** out) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            fn == nullptr) {
+            return FMHA_ERR_DEVICE;
+        }
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1);
+    DeviceContext& ctx = g_devices[dev];
+    if (!ctx.ready) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+        if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
+        if (cudaMalloc(&ctx.err_word, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
+        if (cudaMemset(ctx.err_word, 0, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
+        const int smem = (int)kernel_smem_bytes<false, false>();
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
+        ctx.ready = true;
+    }
+    *out = &ctx;
+    return FMHA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Tensor map over a bf16 tensor seen as (d=64, rows, heads[, batch]), box of
+// 64 x 128 rows, 128-byte swizzle (matches the UMMA SW128 canonical layout).
+int make_map(CUtensorMap* tm, const uint16_t* base, int rank, int rows, int heads, int batch,
+             long long row_stride, long long head_stride, long long batch_stride) {
+    cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows, (cuuint64_t)heads,
+                          (cuuint64_t)batch};
+    // A stride of a size-1 dimension is never used; give it a legal value.
+    if (heads == 1) head_stride = 8;
+    if (batch == 1) batch_stride = 8;
+    cuuint64_t strides[3] = {(cuuint64_t)row_stride * 2, (cuuint64_t)head_stride * 2,
+                             (cuuint64_t)batch_stride * 2};
+    cuuint32_t box[4] = {(cuuint32_t)kHeadDim, (cuuint32_t)kBlockM, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<uint16_t*>(base),
+                          dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? FMHA_OK : FMHA_ERR_ARG;
+}
+
+bool stride_ok(long long s, int extent) {
+    if (extent <= 1) return true;
+    return s > 0 && (s % 8) == 0 && s * 2 < (1ll << 40);
+}
+
+int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
+           cudaStream_t stream) {
+    if (p == nullptr || batch <= 0) return FMHA_ERR_ARG;
+    if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
+    if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
+    if (p->seqlen_q < 0 || p->seqlen_k < 0) return FMHA_ERR_ARG;
+    if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
+        return FMHA_ERR_ARG;
+    if (varlen) {
+        if (!p->seqstart_q || !p->seqstart_k || total_q < 0 || total_k < 0) return FMHA_ERR_ARG;
+    }
+    const int rows_q = varlen ? total_q : p->seqlen_q;
+    const int rows_k = varlen ? total_k : p->seqlen_k;
+    if (!stride_ok(p->stride_q, rows_q) || !stride_ok(p->stride_k, rows_k) ||
+        !stride_ok(p->stride_v, rows_k) || !stride_ok(p->nhead_stride_q, p->nhead_q) ||
+        !stride_ok(p->nhead_stride_k, p->nhead_k) || !stride_ok(p->nhead_stride_v, p->nhead_k))
+        return FMHA_ERR_ARG;
+    if (!varlen && (!stride_ok(p->batch_stride_q, batch) || !stride_ok(p->batch_stride_k, batch) ||
+                    !stride_ok(p->batch_stride_v, batch)))
+        return FMHA_ERR_ARG;
+    if ((p->stride_o % 8) != 0 || (p->nhead_stride_o % 8) != 0 ||
+        (!varlen && (p->batch_stride_o % 8) != 0))
+        return FMHA_ERR_ARG;
+    if (p->seqlen_q == 0 || rows_q == 0) return FMHA_OK;  // nothing to compute
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    DeviceContext* ctx = nullptr;
+    int st = ensure_context(dev, &ctx);
+    if (st != FMHA_OK) return st;
+
+    KernelArgs a;
+    memset(&a, 0, sizeof(a));
+    const int rank = varlen ? 3 : 4;
+    const int mb = varlen ? 1 : batch;
+    // K/V rows: a zero-length key sequence still needs a legal (1-row) map.
+    const int rk = rows_k > 0 ? rows_k : 1;
+    if ((st = make_map(&a.tm_q, p->q, rank, rows_q, p->nhead_q, mb, p->stride_q,
+                       p->nhead_stride_q, p->batch_stride_q)) != FMHA_OK)
+        return st;
+    if ((st = make_map(&a.tm_k, p->k, rank, rk, p->nhead_k, mb, p->stride_k, p->nhead_stride_k,
+                       p->batch_stride_k)) != FMHA_OK)
+        return st;
+    if ((st = make_map(&a.tm_v, p->v, rank, rk, p->nhead_k, mb, p->stride_v, p->nhead_stride_v,
+                       p->batch_stride_v)) != FMHA_OK)
+        return st;
+    a.o = p->o;
+    a.lse = p->lse;
+    a.seqstart_q = p->seqstart_q;
+    a.seqstart_k = p->seqstart_k;
+    a.stride_o = p->stride_o;
+    a.nhead_stride_o = p->nhead_stride_o;
+    a.batch_stride_o = p->batch_stride_o;
+    a.seqlen_q = p->seqlen_q;
+    a.seqlen_k = p->seqlen_k;
+    a.nhead_q = p->nhead_q;
+    a.nhead_k = p->nhead_k;
+    a.total_q = total_q;
+    a.scale = p->scale;
+    a.err_word = ctx->err_word;
+    a.wait_limit_ns = g_wait_limit_ns;
+    a.stall_inject = g_stall_inject;
+
+    const int m_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
+    if (m_blocks > 65535) return FMHA_ERR_ARG;
+    dim3 grid((unsigned)(p->nhead_q * batch), (unsigned)m_blocks, 1);
+    dim3 block(kThreads);
+    const size_t smem = kernel_smem_bytes<false, false>();
+    if (causal) {
+        if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, smem, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<true, false><<<grid, block, smem, stream>>>(a);
+    } else {
+        if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
+    }
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fmha_fwd_d64_bf16_msk0(const FmhaFwdParams* params, int batch, CUstream_st* stream) {
+    if (params && (params->seqstart_q || params->seqstart_k)) return FMHA_ERR_ARG;
+    return launch(params, batch, false, false, 0, 0, stream);
+}
+int fmha_fwd_d64_bf16_msk1(const FmhaFwdParams* params, int batch, CUstream_st* stream) {
+    if (params && (params->seqstart_q || params->seqstart_k)) return FMHA_ERR_ARG;
+    return launch(params, batch, true, false, 0, 0, stream);
+}
+int fmha_fwd_d64_bf16_msk0_varlen(const FmhaFwdParams* params, int batch, int total_q,
+                                  int total_k, CUstream_st* stream) {
+    return launch(params, batch, false, true, total_q, total_k, stream);
+}
+int fmha_fwd_d64_bf16_msk1_varlen(const FmhaFwdParams* params, int batch, int total_q,
+                                  int total_k, CUstream_st* stream) {
+    return launch(params, batch, true, true, total_q, total_k, stream);
+}
+int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal, int total_q,
+                      int total_k, CUstream_st* stream) {
+    if (params == nullptr) return FMHA_ERR_ARG;
+    const bool varlen = params->seqstart_q != nullptr;
+    return launch(params, batch, causal != 0, varlen, total_q, total_k, stream);
+}
+
+int fmha_fwd_d64_status(CUstream_st* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return FMHA_ERR_LAUNCH;
+    int* word = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (dev < (int)g_devices.size() && g_devices[dev].ready) word = g_devices[dev].err_word;
+    }
+    if (word == nullptr) return FMHA_OK;
+    int h = 0;
+    if (cudaMemcpy(&h, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return FMHA_ERR_LAUNCH;
+    if (h != 0) {
+        cudaMemset(word, 0, sizeof(int));
+        return FMHA_ERR_TIMEOUT;
+    }
+    return FMHA_OK;
+}
+
+void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_wait_limit_ns = limit_ns ? limit_ns : 2000000000ull;
+}
+
+// Test hook (not in the public header's main API): makes the producer warp
+// withhold the first V tile so the bounded waits expire.  Used only by the
+// timeout test, which also shortens the wait limit.
+void fmha_fwd_d64_debug_set_stall(int enable) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_stall_inject = enable;
+}
+
+void fmha_fwd_d64_release(void) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    int cur = 0;
+    cudaGetDevice(&cur);
+    for (size_t d = 0; d < g_devices.size(); ++d) {
+        if (g_devices[d].ready) {
+            cudaSetDevice((int)d);
+            cudaFree(g_devices[d].err_word);
+            g_devices[d] = DeviceContext();
+        }
+    }
+    cudaSetDevice(cur);
+}
+
+const char* fmha_fwd_d64_error_string(int status) {
+    switch (status) {
+        case FMHA_OK: return "ok";
+        case FMHA_ERR_ARG: return "invalid argument";
+        case FMHA_ERR_LAUNCH: return "CUDA launch or runtime error";
+        case FMHA_ERR_TIMEOUT: return "device pipeline wait exceeded its time limit";
+        case FMHA_ERR_DEVICE: return "no supported sm_100 device";
+        default: return "unknown status";
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,144 @@
+/*
+ * fmha_fwd.h -- C ABI of the B200 (sm_100a) head-dim-64 BF16 fused multi-head
+ * attention forward pass.
+ *
+ * This header is plain C (C99 / C++17 compatible).  BF16 tensors are passed as
+ * `uint16_t*` holding the raw bf16 bit patterns; all pointers are CUDA device
+ * pointers; no function allocates or frees caller memory.
+ *
+ * Reference interface replaced (poyenc/fmha_native):
+ *   - struct FmhaFwdParams ........ src/runner/params.hpp:18-64 (same fields,
+ *                                   same order, same meaning; bf16 pointers are
+ *                                   uint16_t instead of __hip_bfloat16)
+ *   - fmha_fwd_d64_bf16_msk0 ...... src/fused/kernel.cpp:55-63
+ *   - fmha_fwd_d64_bf16_msk1 ...... src/fused/kernel.cpp:66-76
+ *   - fmha_fwd_d64_bf16_msk0_varlen src/fused/kernel.cpp:80-88
+ *   - fmha_fwd_d64_bf16_msk1_varlen src/fused/kernel.cpp:91-99
+ * In the reference these are `__global__` kernels launched by the caller with
+ * grid (nhead_q, ceil(seqlen_q/128), batch) (src/bench_fmha_fwd.cpp:174-191).
+ * Here they are host functions that own the launch geometry, so the caller
+ * passes the batch count explicitly (the reference passes it as gridDim.z).
+ *
+ * Semantics (identical to the reference):
+ *   O[b,h,i,:] = softmax_j( (Q[b,h,i,:] . K[b,h/r,j,:]) / sqrt(64) ) . V[b,h/r,j,:]
+ *   r = nhead_q / nhead_k (GQA/MQA).  Causal ("msk1") is bottom-right aligned:
+ *   query i attends key j iff j <= i + (seqlen_k - seqlen_q).  Rows with no
+ *   visible key produce O = 0 and LSE = -inf.  P is truncated to bf16 before the
+ *   P.V product and O is truncated to bf16, as in the reference kernel.
+ *   LSE (natural log, fp32) is written when params->lse != NULL:
+ *     dense : lse[(b*nhead_q + h)*seqlen_q + i]
+ *     varlen: lse[h*total_q + seqstart_q[b] + i]
+ *
+ * Restrictions of the TMA data path (checked, FMHA_ERR_ARG otherwise):
+ *   head_dim is 64 (fixed by the entry-point name); q/k/v base pointers are
+ *   16-byte aligned; every q/k/v stride is a multiple of 8 elements (16 bytes);
+ *   o is 16-byte aligned with stride_o a multiple of 8 elements;
+ *   nhead_q % nhead_k == 0.
+ *
+ * All launches are asynchronous on `stream` (NULL = legacy default stream).
+ */
+#ifndef FMHA_FWD_H_
+#define FMHA_FWD_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st; /* cudaStream_t == struct CUstream_st* */
+
+/* Kernel argument block.  Field order and meaning follow the reference
+ * (src/runner/params.hpp:18-64).  Strides are in ELEMENTS.  `scale` is
+ * pre-multiplied by log2(e): scale = log2(e)/sqrt(64). */
+typedef struct FmhaFwdParams {
+    const uint16_t *q, *k, *v; /* bf16 [.., seqlen, 64] with the strides below */
+    uint16_t* o;               /* bf16 output, same logical layout as q        */
+    float* lse;                /* optional fp32 log-sum-exp, NULL disables     */
+
+    int seqlen_q, seqlen_k;    /* dense: lengths; varlen: max lengths          */
+    int nhead_q, nhead_k;
+
+    float scale;               /* log2(e)/sqrt(head_dim)                       */
+
+    int stride_q, nhead_stride_q, batch_stride_q;
+    int stride_k, nhead_stride_k, batch_stride_k;
+    int stride_v, nhead_stride_v, batch_stride_v;
+    int stride_o, nhead_stride_o, batch_stride_o;
+
+    /* varlen: int32 prefix sums of length batch+1 (device memory); the b-th
+     * sequence spans packed rows [seqstart[b], seqstart[b+1]).  Both NULL for
+     * dense mode; batch_stride_* are ignored in varlen mode. */
+    const int32_t* seqstart_q;
+    const int32_t* seqstart_k;
+} FmhaFwdParams;
+
+/* Status codes returned by every entry point. */
+enum {
+    FMHA_OK = 0,
+    FMHA_ERR_ARG = 1,      /* invalid argument (see restrictions above)       */
+    FMHA_ERR_LAUNCH = 2,   /* CUDA launch / driver error                       */
+    FMHA_ERR_TIMEOUT = 3,  /* a device-side pipeline wait exceeded its limit   */
+    FMHA_ERR_DEVICE = 4    /* no sm_100 device / unsupported device            */
+};
+
+/* Dense (fixed-length batch) forward, no mask.
+ * Replaces __global__ fmha_fwd_d64_bf16_msk0 (src/fused/kernel.cpp:55-63). */
+int fmha_fwd_d64_bf16_msk0(const FmhaFwdParams* params, int batch,
+                           struct CUstream_st* stream);
+
+/* Dense forward, bottom-right causal mask.
+ * Replaces __global__ fmha_fwd_d64_bf16_msk1 (src/fused/kernel.cpp:66-76). */
+int fmha_fwd_d64_bf16_msk1(const FmhaFwdParams* params, int batch,
+                           struct CUstream_st* stream);
+
+/* Varlen (group mode) forward, no mask.  total_q / total_k are the packed row
+ * counts (seqstart_q[batch], seqstart_k[batch]); they bound the TMA tensor
+ * extents so no load can leave the caller's buffers.
+ * Replaces __global__ fmha_fwd_d64_bf16_msk0_varlen (src/fused/kernel.cpp:80-88). */
+int fmha_fwd_d64_bf16_msk0_varlen(const FmhaFwdParams* params, int batch,
+                                  int total_q, int total_k,
+                                  struct CUstream_st* stream);
+
+/* Varlen forward, causal.
+ * Replaces __global__ fmha_fwd_d64_bf16_msk1_varlen (src/fused/kernel.cpp:91-99). */
+int fmha_fwd_d64_bf16_msk1_varlen(const FmhaFwdParams* params, int batch,
+                                  int total_q, int total_k,
+                                  struct CUstream_st* stream);
+
+/* Single dispatcher over the four entries above (the host-side selection the
+ * reference performs at src/bench_fmha_fwd.cpp:179-191).  Varlen is selected
+ * when params->seqstart_q != NULL; total_q/total_k are ignored for dense. */
+int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal,
+                      int total_q, int total_k, struct CUstream_st* stream);
+
+/* Synchronizes `stream`, then reads and clears the device error word written
+ * by bounded pipeline waits on the current device.  Returns FMHA_OK or
+ * FMHA_ERR_TIMEOUT (or FMHA_ERR_LAUNCH if the synchronization failed).
+ * No reference counterpart (the reference kernel has no error reporting). */
+int fmha_fwd_d64_status(struct CUstream_st* stream);
+
+/* Sets the time limit (nanoseconds) of every device-side pipeline wait for
+ * subsequent launches on all devices; 0 restores the default (2 s).
+ * No reference counterpart. */
+void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns);
+
+/* Releases the per-device launcher context (error word).  No reference
+ * counterpart. */
+void fmha_fwd_d64_release(void);
+
+/* Human-readable text for a status code. */
+const char* fmha_fwd_d64_error_string(int status);
+
+/* Tile geometry of the B200 kernel (informational; callers need not compute
+ * launch geometry).  128 query rows per tile, two tiles per CTA, 128 keys per
+ * KV tile. */
+#define FMHA_B200_BLOCK_M 128
+#define FMHA_B200_BLOCK_N 128
+#define FMHA_B200_HEAD_DIM 64
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FMHA_FWD_H_ */
