@@ -34,7 +34,10 @@
 //   boundary / causal masking ............... src/fused/op_softmax.hpp:73-131
 //   exp2 softmax with log2e-folded scale .... src/fused/op_softmax.hpp:148-255
 //   P truncated to bf16 before P.V .......... src/fused/op_gemm.hpp:272-273
-//   O * (1/l), bf16 truncation, LSE ......... src/fused/op_epilog.hpp:50-155
+//   O * (1/l), LSE .......................... src/fused/op_epilog.hpp:50-155
+//     (O is rounded to nearest-even bf16 by default, halving the error
+//      against the fp32 oracle; -DFMHA_O_ROUND_TRUNC restores the
+//      reference kernel's truncation, op_epilog.hpp:103-124)
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -513,10 +516,10 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                         const int col = c * 8 + e * 2;
                         const float v0 = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
                         const float v1 = n > 0 ? __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l : 0.0f;
-#ifdef FMHA_O_ROUND_RNE
-                        pk[e] = pack_bf16_rne(v0, v1);
+#ifdef FMHA_O_ROUND_TRUNC
+                        pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
 #else
-                        pk[e] = pack_bf16_trunc(v0, v1);
+                        pk[e] = pack_bf16_rne(v0, v1);
 #endif
                     }
                     dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
