@@ -67,8 +67,9 @@ constexpr int kThreads = 320;
 constexpr int kWarpLoad = 8;
 constexpr int kWarpMma = 9;
 constexpr uint32_t kTmemCols = 512;
-__host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i / P_i
-__host__ __device__ constexpr uint32_t col_o(int i) { return 256u + i * 64u; }  // O_i
+__host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i (fp32)
+__host__ __device__ constexpr uint32_t col_o(int i) { return 256u + i * 64u; }  // O_i (fp32)
+__host__ __device__ constexpr uint32_t col_p(int i) { return 384u + i * 64u; }  // P_i (bf16x2)
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
@@ -102,8 +103,10 @@ struct alignas(1024) SharedStorage {
     uint64_t bar_q[kTilesPerCta];
     uint64_t bar_full[kStages];
     uint64_t bar_empty[kStages];
-    uint64_t bar_s[kTilesPerCta];
-    uint64_t bar_p[kTilesPerCta];
+    uint64_t bar_s[kTilesPerCta];      // S_i written (MMA commit)
+    uint64_t bar_sfree[kTilesPerCta];  // S_i read into registers (128 arrivals)
+    uint64_t bar_p[kTilesPerCta];      // P_i written, O_i rescaled (128 arrivals)
+    uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
     uint64_t bar_o[kTilesPerCta];
     uint64_t bar_drain;
     uint32_t tmem_base;
@@ -219,7 +222,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         for (int i = 0; i < kTilesPerCta; ++i) {
             mbar_init(smem_u32(&sm.bar_q[i]), 1);
             mbar_init(smem_u32(&sm.bar_s[i]), 1);
+            mbar_init(smem_u32(&sm.bar_sfree[i]), kBlockM);
             mbar_init(smem_u32(&sm.bar_p[i]), kBlockM);
+            mbar_init(smem_u32(&sm.bar_pv[i]), 1);
             mbar_init(smem_u32(&sm.bar_o[i]), 1);
         }
         for (int s = 0; s < kStages; ++s) {
@@ -323,7 +328,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 #pragma unroll
                 for (int kk = 0; kk < kBlockN / 16; ++kk) {
                     const uint64_t db = smem_desc_sw128(vaddr + kk * 2048, 0, 1024);
-                    mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, db, idesc_pv,
+                    mma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, db, idesc_pv,
                            (accumulate || kk > 0) ? 1u : 0u);
                 }
             };
@@ -344,36 +349,43 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     mma_commit(smem_u32(&sm.bar_empty[slot_of(0)]));
                 }
             }
+            // Steady state, per KV tile j:
+            //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
+            //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
             for (int j = 0; j < n_max && ok; ++j) {
                 const int v_idx = 2 * j + 1;
                 const int k_idx = 2 * j + 2;
+                bool k_used = false;
+                for (int i = 0; i < kTilesPerCta; ++i) {
+                    if (j + 1 >= w.n_kv[i]) continue;
+                    if (!k_used) {
+                        ok = wait_phase(smem_u32(&sm.bar_full[slot_of(k_idx)]), full_parity(k_idx),
+                                        abort_flag, a, kErrTimeoutMma);
+                        if (!ok) break;
+                        k_used = true;
+                    }
+                    ok = wait_phase(smem_u32(&sm.bar_sfree[i]), j & 1, abort_flag, a, kErrTimeoutMma);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s(i, slot_of(k_idx));
+                    mma_commit(smem_u32(&sm.bar_s[i]));
+                }
+                if (!ok) break;
+                if (k_used) mma_commit(smem_u32(&sm.bar_empty[slot_of(k_idx)]));
                 ok = wait_phase(smem_u32(&sm.bar_full[slot_of(v_idx)]), full_parity(v_idx),
                                 abort_flag, a, kErrTimeoutMma);
                 if (!ok) break;
-                tc_fence_after();
-                bool k_ready = false;
                 for (int i = 0; i < kTilesPerCta; ++i) {
                     if (j >= w.n_kv[i]) continue;
                     ok = wait_phase(smem_u32(&sm.bar_p[i]), j & 1, abort_flag, a, kErrTimeoutMma);
                     if (!ok) break;
                     tc_fence_after();
                     issue_pv(i, slot_of(v_idx), j > 0);
+                    mma_commit(smem_u32(&sm.bar_pv[i]));
                     if (j == w.n_kv[i] - 1) mma_commit(smem_u32(&sm.bar_o[i]));
-                    if (j + 1 < w.n_kv[i]) {
-                        if (!k_ready) {
-                            ok = wait_phase(smem_u32(&sm.bar_full[slot_of(k_idx)]),
-                                            full_parity(k_idx), abort_flag, a, kErrTimeoutMma);
-                            if (!ok) break;
-                            tc_fence_after();
-                            k_ready = true;
-                        }
-                        issue_s(i, slot_of(k_idx));
-                        mma_commit(smem_u32(&sm.bar_s[i]));
-                    }
                 }
                 if (!ok) break;
                 mma_commit(smem_u32(&sm.bar_empty[slot_of(v_idx)]));
-                if (k_ready) mma_commit(smem_u32(&sm.bar_empty[slot_of(k_idx)]));
             }
             // All MMAs this thread issued must finish before TMEM is freed.
             mma_commit(smem_u32(&sm.bar_drain));
@@ -399,6 +411,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         float l_run = 0.0f;       // running sum of un-normalised P
         bool ok = true;
 
+        const uint32_t tP = tmem + lane_base + col_p(i);
         for (int j = 0; j < n; ++j) {
             bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
             if (!__all_sync(0xffffffffu, got)) {
@@ -412,6 +425,10 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 4; ++c) reg_fence(r[c]);
+            // S_i now lives in registers: the MMA warp may overwrite it with
+            // S_i(j+1) while this group computes P_i(j).
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sm.bar_sfree[i]));
 
             const int k0 = j * kBlockN;
             const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
@@ -423,18 +440,20 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     for (int e = 0; e < 32; ++e)
                         if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
             }
+            // Row max: 8 independent 3-input-max chains.
             float mx[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int q = c * 2 + (e >> 4);
-                    if ((e & 15) != 0) mx[q] = fmaxf(mx[q], __uint_as_float(r[c][e]));
-                }
-            const float row_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                        fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                for (int e = 1; e < 15; e += 2)
+                    mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+                mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
+            }
+            const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                                        fmaxf(mx[6], mx[7]));
             const float m_new = fmaxf(m_run, row_max);
             const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
             float alpha = 1.0f;
@@ -442,38 +461,55 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 alpha = ex2_approx((m_run - m_new) * scale);
                 m_run = m_new;
             }
-            l_run *= alpha;
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const float neg_ms = -m_use * scale;
-            float sum[8];
+            const float2 scale2 = make_float2(scale, scale);
+            const float2 neg2 = make_float2(neg_ms, neg_ms);
+            float2 sum[4];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) sum[q] = 0.0f;
+            for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
             uint32_t p[2][32];
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2_approx(fmaf(__uint_as_float(r[c][e]), scale, neg_ms));
-                    const float p1 = ex2_approx(fmaf(__uint_as_float(r[c][e + 1]), scale, neg_ms));
-                    const int q = (c * 2 + (e >> 4));
-                    sum[q] += p0 + p1;
-                    p[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16_trunc(p0, p1);
+                    const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
+                                                       __uint_as_float(r[c][e + 1])),
+                                           scale2, neg2);
+                    const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                    sum[(e >> 1) & 3] = fadd2(sum[(e >> 1) & 3], pp);
+                    p[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16_trunc(pp.x, pp.y);
                 }
-            l_run += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
-            tmem_st32(tS, p[0]);
-            tmem_st32(tS + 32, p[1]);
+            const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
+            l_run = fmaf(l_run, alpha, s01.x + s01.y);
+
+            if (j > 0) {
+                // P_i(j-1) must be consumed (and O_i settled) before P_i(j) and the
+                // O_i rescale are written.
+                got = wait_phase(smem_u32(&sm.bar_pv[i]), (j - 1) & 1, abort_flag, a,
+                                 kErrTimeoutSoftmax);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+            tmem_st32(tP, p[0]);
+            tmem_st32(tP + 32, p[1]);
             if (j > 0 && __any_sync(0xffffffffu, upd)) {
-                // O_i is quiescent here: s_full for S_i(j) was committed after
-                // O_i += P_i(j-1) V_{j-1}, and O_i += P_i(j) V_j waits for p_full.
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
                     uint32_t o[32];
                     tmem_ld32(tO + c * 32, o);
                     tmem_wait_ld();
                     reg_fence(o);
+                    const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    for (int e = 0; e < 32; e += 2) {
+                        const float2 v2 = fmul2(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
+                        o[e] = __float_as_uint(v2.x);
+                        o[e + 1] = __float_as_uint(v2.y);
+                    }
                     tmem_st32(tO + c * 32, o);
                 }
             }

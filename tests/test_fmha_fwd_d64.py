@@ -94,5 +94,5 @@ def test_known_answer_closed_form(cuda_device, sq, sk):
                                   strides_k=(D, sk * D, sk * D), strides_v=(D, sk * D, sk * D),
                                   out_shape=(1, 1, sq, D), strides_o=(D, sq * D, sq * D))
     v_ = O.compare(o_k, o_ref, lse.cpu().numpy(), lse_ref)
-    # V is in [1, 2): one bf16 ulp there is 2^-7, so the abs bar is the ulp.
-    assert v_["max_abs"] <= 2.0 ** -7 and v_["lse_pass"], v_
+    # O lies in [1, 2) here (bf16 ulp 2^-7): the BASELINE bar applies.
+    assert v_["baseline_pass"] and v_["lse_pass"], v_
