@@ -63,7 +63,12 @@ constexpr int kTilesPerCta = 2;         // query tiles per CTA
 constexpr int kRowsPerCta = kBlockM * kTilesPerCta;
 constexpr int kStages = 6;              // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;            // 3 warpgroups
+// Register split (setmaxnreg): the CTA launches with 384 x 168 registers;
+// the two softmax groups take 224 each, the producer/MMA group keeps 56:
+// 128 * (224 + 224 + 56) == 384 * 168.
+constexpr int kRegsSoftmax = 224;
+constexpr int kRegsControl = 56;
 constexpr int kWarpLoad = 8;
 constexpr int kWarpMma = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -116,7 +121,7 @@ struct alignas(1024) SharedStorage {
 // Bounded wait on an mbarrier phase.  Returns false if the CTA-wide abort
 // flag is raised or the time limit expires (then it raises the flag and
 // records `code` in the device error word).
-__device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+__device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                         const KernelArgs& a, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -135,7 +140,7 @@ __device__ __noinline__ bool wait_phase(uint32_t bar, uint32_t parity, volatile 
 
 // Bounded wait used only while tearing down after an abort: ignores the
 // abort flag, gives up silently after the time limit.
-__device__ __noinline__ void drain_phase(uint32_t bar, uint32_t parity, const KernelArgs& a) {
+__device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const KernelArgs& a) {
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity)) {
         if (globaltimer_ns() - t0 > a.wait_limit_ns) return;
@@ -246,6 +251,8 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 
     const int n_max = max(w.n_kv[0], w.n_kv[1]);
 
+    if (warp >= 8) {
+    regs_dec<kRegsControl>();
     if (warp == kWarpLoad) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -392,7 +399,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             drain_phase(smem_u32(&sm.bar_drain), 0, a);
         }
         __syncwarp();
+    }
     } else {
+        regs_inc<kRegsSoftmax>();
         // ------------------------------------------------------ softmax groups
         const int i = warp >> 2;                    // query tile of this group
         const int t = threadIdx.x & (kBlockM - 1);  // row inside the tile == TMEM lane
