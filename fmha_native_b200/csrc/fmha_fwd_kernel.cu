@@ -65,10 +65,10 @@ constexpr int kStages = 6;              // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
 constexpr int kThreads = 384;            // 3 warpgroups
 // Register split (setmaxnreg): the CTA launches with 384 x 168 registers;
-// the two softmax groups take 224 each, the producer/MMA group keeps 56:
-// 128 * (224 + 224 + 56) == 384 * 168.
-constexpr int kRegsSoftmax = 224;
-constexpr int kRegsControl = 56;
+// the two softmax groups take 208 each, the producer/MMA group 88:
+// 128 * (208 + 208 + 88) == 63488 <= 384 * 168.
+constexpr int kRegsSoftmax = 208;
+constexpr int kRegsControl = 88;
 constexpr int kWarpLoad = 8;
 constexpr int kWarpMma = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -100,7 +100,20 @@ struct KernelArgs {
     int* err_word;
     unsigned long long wait_limit_ns;
     int stall_inject;          // test hook: producer withholds the first V tile
+    unsigned long long* trace; // FMHA_TRACE builds: per-event clock64 of CTA (0,0)
 };
+
+// Pipeline event timestamps (diagnostic builds only, -DFMHA_TRACE): slot
+// 0/1 = softmax group 0/1 (thread 0), 2 = MMA issuer; 8 events per KV tile.
+#ifdef FMHA_TRACE
+#define TRACE_EV(slot, j, ev)                                                          \
+    do {                                                                               \
+        if (a.trace && blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64)                 \
+            a.trace[((slot) * 64 + (j)) * 8 + (ev)] = clock64();                       \
+    } while (0)
+#else
+#define TRACE_EV(slot, j, ev) do { } while (0)
+#endif
 
 struct alignas(1024) SharedStorage {
     uint8_t q[kTilesPerCta][kTileBytes];
@@ -249,7 +262,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    const int n_max = max(w.n_kv[0], w.n_kv[1]);
+    // Per-tile KV counts as scalars (a runtime-indexed array would live in
+    // local memory).
+    const int n_kv0 = w.n_kv[0];
+    const int n_kv1 = w.n_kv[1];
+    auto n_kv = [n_kv0, n_kv1](int i) { return i == 0 ? n_kv0 : n_kv1; };
+    const int n_max = max(n_kv0, n_kv1);
 
     if (warp >= 8) {
     regs_dec<kRegsControl>();
@@ -263,7 +281,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             const uint64_t pol_kv = l2_policy_evict_last();
             const int qbatch = kVarlen ? 0 : w.b;
             for (int i = 0; i < kTilesPerCta; ++i) {
-                if (w.n_kv[i] == 0) continue;
+                if (n_kv(i) == 0) continue;
                 const uint32_t bar = smem_u32(&sm.bar_q[i]);
                 mbar_arrive_expect_tx(bar, kTileBytes);
                 tma_load_rows<kVarlen>(smem_u32(sm.q[i]), &a.tm_q, bar,
@@ -296,7 +314,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             if (!ok || *abort_flag) {
                 // Let every copy this warp started land before the CTA exits.
                 for (int i = 0; i < kTilesPerCta; ++i)
-                    if (w.n_kv[i] > 0) drain_phase(smem_u32(&sm.bar_q[i]), 0, a);
+                    if (n_kv(i) > 0) drain_phase(smem_u32(&sm.bar_q[i]), 0, a);
                 for (int idx = max(0, issued - kStages); idx < issued; ++idx) {
                     if (a.stall_inject && idx == 1) continue;
                     drain_phase(smem_u32(&sm.bar_full[idx % kStages]), (idx / kStages) & 1, a);
@@ -306,98 +324,120 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         __syncwarp();
     } else if (warp == kWarpMma) {
         // ------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc_qk = idesc_bf16_f32(kBlockM, kBlockN, 0, 0);
-            constexpr uint32_t idesc_pv = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
-            const uint32_t q_base[2] = {smem_u32(sm.q[0]), smem_u32(sm.q[1])};
-            const uint32_t kv_base = smem_u32(sm.kv[0]);
-            bool ok = true;
+        // The whole warp walks the schedule (waits included) so it stays
+        // converged; one elected lane issues the tcgen05 instructions.  A
+        // lone-lane issuer costs roughly 1.5-2x more cycles per MMA.
+        const bool leader = elect_one();
+        constexpr uint32_t idesc_qk = idesc_bf16_f32(kBlockM, kBlockN, 0, 0);
+        constexpr uint32_t idesc_pv = idesc_bf16_f32(kBlockM, kHeadDim, 0, 1);
+        const uint32_t kv_base = smem_u32(sm.kv[0]);
+        // Descriptors are linear in the start address (bits 0-13 hold
+        // address >> 4): each operand descriptor is a base descriptor plus a
+        // byte offset >> 4.
+        const uint64_t dq0 = smem_desc_sw128(smem_u32(sm.q[0]), 16, 1024);
+        const uint64_t dk0 = smem_desc_sw128(kv_base, 16, 1024);
+        const uint64_t dv0 = smem_desc_sw128(kv_base, 0, 1024);
+        bool ok = true;
 
-            auto slot_of = [](int idx) { return idx % kStages; };
-            auto full_parity = [](int idx) { return (uint32_t)((idx / kStages) & 1); };
-
-            // S_i = Q_i K^T : M=128, N=128, K=64 as 4 x K16 (32 bytes apart
-            // inside the 128-byte swizzled rows).
-            auto issue_s = [&](int i, int slot) {
-                const uint32_t kaddr = kv_base + slot * kTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-                    const uint64_t da = smem_desc_sw128(q_base[i] + kk * 32, 16, 1024);
-                    const uint64_t db = smem_desc_sw128(kaddr + kk * 32, 16, 1024);
-                    mma_ss(tmem + col_s(i), da, db, idesc_qk, kk > 0);
-                }
-            };
-            // O_i += P_i V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the
-            // TMEM A operand; V is MN-major in shared memory, 16 keys = two
-            // 8-row swizzle atoms = 2048 bytes per step.
-            auto issue_pv = [&](int i, int slot, bool accumulate) {
-                const uint32_t vaddr = kv_base + slot * kTileBytes;
-#pragma unroll
-                for (int kk = 0; kk < kBlockN / 16; ++kk) {
-                    const uint64_t db = smem_desc_sw128(vaddr + kk * 2048, 0, 1024);
-                    mma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, db, idesc_pv,
-                           (accumulate || kk > 0) ? 1u : 0u);
-                }
-            };
-
-            for (int i = 0; i < kTilesPerCta && ok; ++i)
-                if (w.n_kv[i] > 0)
-                    ok = wait_phase(smem_u32(&sm.bar_q[i]), 0, abort_flag, a, kErrTimeoutMma);
-            if (ok && n_max > 0) {
-                ok = wait_phase(smem_u32(&sm.bar_full[slot_of(0)]), full_parity(0), abort_flag, a,
-                                kErrTimeoutMma);
-                if (ok) {
-                    tc_fence_after();
-                    for (int i = 0; i < kTilesPerCta; ++i) {
-                        if (w.n_kv[i] == 0) continue;
-                        issue_s(i, slot_of(0));
-                        mma_commit(smem_u32(&sm.bar_s[i]));
-                    }
-                    mma_commit(smem_u32(&sm.bar_empty[slot_of(0)]));
-                }
+        auto slot_of = [](int idx) { return idx % kStages; };
+        auto full_parity = [](int idx) { return (uint32_t)((idx / kStages) & 1); };
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+            const bool got = wait_phase(smem_u32(bar), parity, abort_flag, a, kErrTimeoutMma);
+            return __all_sync(0xffffffffu, got);
+        };
+        auto commit = [&](uint64_t* bar) {
+            if (leader) mma_commit(smem_u32(bar));
+        };
+        // S_i = Q_i K^T : M=128, N=128, K=64 as 4 x K16, 32 bytes (descriptor
+        // +2) apart inside the 128-byte swizzled rows.
+        auto issue_s = [&](int i, int slot) {
+            const uint64_t da = dq0 + (uint64_t)(i * (kTileBytes >> 4));
+            const uint64_t db = dk0 + (uint64_t)(slot * (kTileBytes >> 4));
+            const uint32_t d = tmem + col_s(i);
+            if (leader) {
+                mma_ss(d, da, db, idesc_qk, 0u);
+                mma_ss(d, da + 2, db + 2, idesc_qk, 1u);
+                mma_ss(d, da + 4, db + 4, idesc_qk, 1u);
+                mma_ss(d, da + 6, db + 6, idesc_qk, 1u);
             }
-            // Steady state, per KV tile j:
-            //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
-            //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
-            for (int j = 0; j < n_max && ok; ++j) {
-                const int v_idx = 2 * j + 1;
-                const int k_idx = 2 * j + 2;
-                bool k_used = false;
-                for (int i = 0; i < kTilesPerCta; ++i) {
-                    if (j + 1 >= w.n_kv[i]) continue;
-                    if (!k_used) {
-                        ok = wait_phase(smem_u32(&sm.bar_full[slot_of(k_idx)]), full_parity(k_idx),
-                                        abort_flag, a, kErrTimeoutMma);
-                        if (!ok) break;
-                        k_used = true;
-                    }
-                    ok = wait_phase(smem_u32(&sm.bar_sfree[i]), j & 1, abort_flag, a, kErrTimeoutMma);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_s(i, slot_of(k_idx));
-                    mma_commit(smem_u32(&sm.bar_s[i]));
-                }
-                if (!ok) break;
-                if (k_used) mma_commit(smem_u32(&sm.bar_empty[slot_of(k_idx)]));
-                ok = wait_phase(smem_u32(&sm.bar_full[slot_of(v_idx)]), full_parity(v_idx),
-                                abort_flag, a, kErrTimeoutMma);
-                if (!ok) break;
-                for (int i = 0; i < kTilesPerCta; ++i) {
-                    if (j >= w.n_kv[i]) continue;
-                    ok = wait_phase(smem_u32(&sm.bar_p[i]), j & 1, abort_flag, a, kErrTimeoutMma);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_pv(i, slot_of(v_idx), j > 0);
-                    mma_commit(smem_u32(&sm.bar_pv[i]));
-                    if (j == w.n_kv[i] - 1) mma_commit(smem_u32(&sm.bar_o[i]));
-                }
-                if (!ok) break;
-                mma_commit(smem_u32(&sm.bar_empty[slot_of(v_idx)]));
+        };
+        // O_i += P_i V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the
+        // TMEM A operand; V is MN-major in shared memory, 16 keys = two 8-row
+        // swizzle atoms = 2048 bytes (descriptor +128) per step.
+        auto issue_pv = [&](int i, int slot, bool accumulate) {
+            const uint64_t db = dv0 + (uint64_t)(slot * (kTileBytes >> 4));
+            const uint32_t d = tmem + col_o(i);
+            const uint32_t pa = tmem + col_p(i);
+            if (leader) {
+                mma_ts(d, pa, db, idesc_pv, accumulate ? 1u : 0u);
+#pragma unroll
+                for (int kk = 1; kk < kBlockN / 16; ++kk)
+                    mma_ts(d, pa + kk * 8, db + (uint64_t)(kk * 128), idesc_pv, 1u);
             }
-            // All MMAs this thread issued must finish before TMEM is freed.
-            mma_commit(smem_u32(&sm.bar_drain));
-            drain_phase(smem_u32(&sm.bar_drain), 0, a);
+        };
+
+        for (int i = 0; i < kTilesPerCta && ok; ++i)
+            if (n_kv(i) > 0) ok = wait_all(&sm.bar_q[i], 0);
+        if (ok && n_max > 0) {
+            ok = wait_all(&sm.bar_full[slot_of(0)], full_parity(0));
+            if (ok) {
+                tc_fence_after();
+                for (int i = 0; i < kTilesPerCta; ++i) {
+                    if (n_kv(i) == 0) continue;
+                    issue_s(i, slot_of(0));
+                    commit(&sm.bar_s[i]);
+                }
+                commit(&sm.bar_empty[slot_of(0)]);
+            }
         }
+        // Steady state, per KV tile j:
+        //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
+        //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
+        for (int j = 0; j < n_max && ok; ++j) {
+            const int v_idx = 2 * j + 1;
+            const int k_idx = 2 * j + 2;
+            bool k_used = false;
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (j + 1 >= n_kv(i)) continue;
+                if (!k_used) {
+                    ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
+                    if (!ok) break;
+                    TRACE_EV(2, j, 4);
+                    k_used = true;
+                }
+                ok = wait_all(&sm.bar_sfree[i], j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                TRACE_EV(2, j, i);
+                issue_s(i, slot_of(k_idx));
+                TRACE_EV(3, j, i * 2);
+                commit(&sm.bar_s[i]);
+                TRACE_EV(3, j, i * 2 + 1);
+            }
+            if (!ok) break;
+            if (k_used) commit(&sm.bar_empty[slot_of(k_idx)]);
+            TRACE_EV(2, j, 7);
+            ok = wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx));
+            if (!ok) break;
+            TRACE_EV(2, j, 5);
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (j >= n_kv(i)) continue;
+                ok = wait_all(&sm.bar_p[i], j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                TRACE_EV(2, j, 2 + i);
+                issue_pv(i, slot_of(v_idx), j > 0);
+                TRACE_EV(3, j, 4 + i * 2);
+                commit(&sm.bar_pv[i]);
+                if (j == n_kv(i) - 1) commit(&sm.bar_o[i]);
+                TRACE_EV(3, j, 5 + i * 2);
+            }
+            if (!ok) break;
+            commit(&sm.bar_empty[slot_of(v_idx)]);
+        }
+        // All MMAs this warp issued must finish before TMEM is freed.
+        commit(&sm.bar_drain);
+        drain_phase(smem_u32(&sm.bar_drain), 0, a);
         __syncwarp();
     }
     } else {
@@ -408,7 +448,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_base + col_s(i);
         const uint32_t tO = tmem + lane_base + col_o(i);
-        const int n = w.n_kv[i];
+        const int n = n_kv(i);
         const int tile_row0 = w.row0 + i * kBlockM;
         const int row = tile_row0 + t;
         const int shift = w.seqlen_k - w.seqlen_q;
@@ -422,7 +462,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 
         const uint32_t tP = tmem + lane_base + col_p(i);
         for (int j = 0; j < n; ++j) {
+            if (t == 0) TRACE_EV(i, j, 0);
             bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
+            if (t == 0) TRACE_EV(i, j, 1);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
                 break;
@@ -438,6 +480,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             // S_i(j+1) while this group computes P_i(j).
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_sfree[i]));
+            if (t == 0) TRACE_EV(i, j, 2);
 
             const int k0 = j * kBlockN;
             const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
@@ -491,6 +534,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
             const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
             l_run = fmaf(l_run, alpha, s01.x + s01.y);
+            if (t == 0) TRACE_EV(i, j, 3);
 
             if (j > 0) {
                 // P_i(j-1) must be consumed (and O_i settled) before P_i(j) and the
@@ -503,6 +547,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
                 tc_fence_after();
             }
+            if (t == 0) TRACE_EV(i, j, 4);
             tmem_st32(tP, p[0]);
             tmem_st32(tP + 32, p[1]);
             if (j > 0 && __any_sync(0xffffffffu, upd)) {
@@ -525,6 +570,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_p[i]));
+            if (t == 0) TRACE_EV(i, j, 5);
         }
 
         // ---------------------------------------------------- epilogue
@@ -607,6 +653,7 @@ std::vector<DeviceContext> g_devices;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 unsigned long long g_wait_limit_ns = 2000000000ull;
 int g_stall_inject = 0;
+unsigned long long* g_trace = nullptr;
 
 template <bool C, bool V>
 constexpr size_t kernel_smem_bytes() {
@@ -738,6 +785,7 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     a.err_word = ctx->err_word;
     a.wait_limit_ns = g_wait_limit_ns;
     a.stall_inject = g_stall_inject;
+    a.trace = g_trace;
 
     const int m_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
     if (m_blocks > 65535) return FMHA_ERR_ARG;
@@ -812,6 +860,13 @@ void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns) {
 void fmha_fwd_d64_debug_set_stall(int enable) {
     std::lock_guard<std::mutex> lock(g_mutex);
     g_stall_inject = enable;
+}
+
+// Diagnostic hook: device buffer (>= 3*64*8 u64) receiving pipeline event
+// timestamps in builds compiled with -DFMHA_TRACE; NULL disables.
+void fmha_fwd_d64_debug_set_trace(void* device_buffer) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_trace = static_cast<unsigned long long*>(device_buffer);
 }
 
 void fmha_fwd_d64_release(void) {
