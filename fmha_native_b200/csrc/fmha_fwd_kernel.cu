@@ -47,6 +47,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/fmha_fwd.h"
@@ -78,6 +79,12 @@ __host__ __device__ constexpr uint32_t col_p(int i) { return 384u + i * 64u; }  
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
+// Pairs (of every 16) whose exp2 runs as a polynomial on the FMA/ALU pipes
+// instead of MUFU (unmasked tiles only).
+#ifndef FMHA_EXP_POLY_PAIRS
+#define FMHA_EXP_POLY_PAIRS 4
+#endif
+constexpr int kExpPolyPairs = FMHA_EXP_POLY_PAIRS;
 
 // Error codes written to the device error word.
 constexpr int kErrTimeoutLoad = 0x101;
@@ -125,6 +132,8 @@ struct alignas(1024) SharedStorage {
     uint64_t bar_sfree[kTilesPerCta];  // S_i read into registers (128 arrivals)
     uint64_t bar_p[kTilesPerCta];      // P_i written, O_i rescaled (128 arrivals)
     uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
+    uint64_t bar_turn[kTilesPerCta];   // exp-phase hand-off between the two
+                                       // softmax groups (one arrival per warp)
     uint64_t bar_o[kTilesPerCta];
     uint64_t bar_drain;
     uint32_t tmem_base;
@@ -243,6 +252,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             mbar_init(smem_u32(&sm.bar_sfree[i]), kBlockM);
             mbar_init(smem_u32(&sm.bar_p[i]), kBlockM);
             mbar_init(smem_u32(&sm.bar_pv[i]), 1);
+            mbar_init(smem_u32(&sm.bar_turn[i]), 4);
             mbar_init(smem_u32(&sm.bar_o[i]), 1);
         }
         for (int s = 0; s < kStages; ++s) {
@@ -515,23 +525,59 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const float neg_ms = -m_use * scale;
+            // The exp loops of the two groups alternate (MUFU is shared per
+            // SM sub-partition): group i starts exp(j) once the other group
+            // finished its exp for the tile before (group 0: exp_1(j-1),
+            // group 1: exp_0(j)), and signals when done.
+#ifndef FMHA_EXP_ALTERNATE
+#define FMHA_EXP_ALTERNATE 0
+#endif
+            if (FMHA_EXP_ALTERNATE) {
+                const int other_n = n_kv(i ^ 1);
+                const int need = i == 0 ? j - 1 : j;  // other group's tile to wait for
+                if (need >= 0 && need < other_n) {
+                    got = wait_phase(smem_u32(&sm.bar_turn[i]), need & 1, abort_flag, a,
+                                     kErrTimeoutSoftmax);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            if (t == 0) TRACE_EV(i, j, 6);
             const float2 scale2 = make_float2(scale, scale);
             const float2 neg2 = make_float2(neg_ms, neg_ms);
             float2 sum[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
             uint32_t p[2][32];
+            // P = exp2(S*scale - m*scale).  On tiles without masking a fixed
+            // share of the pairs (kExpPolyPairs of every 16) runs the
+            // polynomial exp2 on the FMA/ALU pipes, relieving MUFU; masked
+            // tiles (which may hold -inf) use MUFU ex2 only.
+            auto exp_tile = [&](auto poly_tag) {
+                constexpr bool kPoly = decltype(poly_tag)::value;
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
-                                                       __uint_as_float(r[c][e + 1])),
-                                           scale2, neg2);
-                    const float2 pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                    sum[(e >> 1) & 3] = fadd2(sum[(e >> 1) & 3], pp);
-                    p[c >> 1][(c & 1) * 16 + (e >> 1)] = pack_bf16_trunc(pp.x, pp.y);
-                }
+                    for (int e = 0; e < 32; e += 2) {
+                        const int pr = e >> 1;  // pair index in the chunk
+                        const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
+                                                           __uint_as_float(r[c][e + 1])),
+                                               scale2, neg2);
+                        float2 pp;
+                        if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
+                            pp = exp2_poly2(x);
+                        else
+                            pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        sum[pr & 3] = fadd2(sum[pr & 3], pp);
+                        p[c >> 1][(c & 1) * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
+                    }
+            };
+            if (need_mask) exp_tile(std::false_type{});
+            else exp_tile(std::true_type{});
+            __syncwarp();
+            if (FMHA_EXP_ALTERNATE && lane == 0) mbar_arrive(smem_u32(&sm.bar_turn[i ^ 1]));
             const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
             l_run = fmaf(l_run, alpha, s01.x + s01.y);
             if (t == 0) TRACE_EV(i, j, 3);

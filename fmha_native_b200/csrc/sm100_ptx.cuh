@@ -244,6 +244,27 @@ template <int N>
 __device__ __forceinline__ void regs_dec() {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
+// 2^x for a pair on the FMA/ALU pipes instead of MUFU.  x = n + f with
+// n = round(x) (the 1.5*2^23 addition leaves n in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f is a degree-3 minimax polynomial (coefficients from
+// fit_exp2_poly.py, max relative error 7.5e-5) and 2^n is added to its
+// exponent field.  Inputs are clamped to >= -120 so the exponent never
+// underflows; callers use it only where every input is finite.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -120.0f);
+    x.y = fmaxf(x.y, -120.0f);
+    const float2 t = fadd2(x, make_float2(kRound, kRound));
+    const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+    const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+    float2 p = ffma2(make_float2(5.517166853e-02f, 5.517166853e-02f), f,
+                     make_float2(2.426111400e-01f, 2.426111400e-01f));
+    p = ffma2(p, f, make_float2(6.932609677e-01f, 6.932609677e-01f));
+    p = ffma2(p, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // Pack the upper 16 bits of two floats: bf16 truncation of (lo, hi).
 __device__ __forceinline__ uint32_t pack_bf16_trunc(float lo, float hi) {
     uint32_t r;
