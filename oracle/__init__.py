@@ -272,7 +272,8 @@ def compare(o_kern: np.ndarray, o_ref: np.ndarray, lse_kern=None, lse_ref=None) 
         sel = ~np.isnan(lr)
         lk, lr = lk[sel], lr[sel]
         both_ninf = np.isneginf(lk) & np.isneginf(lr)
-        d = np.abs(lk - lr)
+        with np.errstate(invalid="ignore"):
+            d = np.abs(lk - lr)
         d[both_ninf] = 0.0
         d = np.where(np.isnan(d), np.inf, d)
         out["lse_max_abs"] = float(d.max()) if d.size else 0.0
