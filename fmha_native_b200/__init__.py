@@ -45,6 +45,7 @@ ENTRY_POINTS = (
     "fmha_fwd_d64_bf16_msk0_varlen",
     "fmha_fwd_d64_bf16_msk1_varlen",
     "fmha_fwd_d64_bf16",
+    "fmha_fwd_d64_bf16_tiles",
     "fmha_fwd_d64_status",
     "fmha_fwd_d64_set_wait_limit_ns",
     "fmha_fwd_d64_release",
@@ -101,6 +102,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fmha_fwd_d64_bf16.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_void_p]
     lib.fmha_fwd_d64_bf16.restype = ctypes.c_int
+    lib.fmha_fwd_d64_bf16_tiles.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                            ctypes.c_void_p]
+    lib.fmha_fwd_d64_bf16_tiles.restype = ctypes.c_int
     lib.fmha_fwd_d64_status.argtypes = [ctypes.c_void_p]
     lib.fmha_fwd_d64_status.restype = ctypes.c_int
     lib.fmha_fwd_d64_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
@@ -180,6 +185,14 @@ def call_entry(params: FmhaFwdParams, batch: int, causal: bool, varlen: bool,
     return fn(ref, batch, ctypes.c_void_p(stream))
 
 
+def call_tiles(params: FmhaFwdParams, batch: int, causal: bool, tiles_ptr: int, ntiles: int,
+               total_q: int = 0, total_k: int = 0, stream: int = 0) -> int:
+    """Call fmha_fwd_d64_bf16_tiles on a device int32 [ntiles, 2] work list."""
+    lib = load_library()
+    return lib.fmha_fwd_d64_bf16_tiles(ctypes.byref(params), batch, int(causal), total_q, total_k,
+                                       ctypes.c_void_p(tiles_ptr), ntiles, ctypes.c_void_p(stream))
+
+
 def status(stream: int = 0) -> int:
     """Synchronise `stream` and read/clear the device error word."""
     return load_library().fmha_fwd_d64_status(ctypes.c_void_p(stream))
@@ -231,12 +244,15 @@ def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
 
 
 def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: str = "bshd",
-             cu_seqlens_q=None, cu_seqlens_k=None, out=None, lse_out=None, stream=None):
+             cu_seqlens_q=None, cu_seqlens_k=None, out=None, lse_out=None, stream=None,
+             tiles=None):
     """O = softmax(Q K^T / 8) V on the B200 kernel (head_dim 64, bf16).
 
     Dense: q [B,Sq,Hq,64] ("bshd") or [B,Hq,Sq,64] ("bhsd"); varlen: q
     [total,Hq,64] ("thd") or [Hq,total,64] ("htd") with int32 cu_seqlens.
     Returns O (and fp32 LSE [B,Hq,Sq] / [Hq,total] when return_lse).
+    `tiles`: optional device int32 [n, 2] list of query blocks to compute
+    (fmha_native_b200.shard); other rows of `out` are left untouched.
     """
     import torch
 
@@ -259,5 +275,10 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
                               dtype=torch.float32)
     params, batch, tq, tk = params_from_tensors(q, k, v, o, lse, layout, cu_seqlens_q, cu_seqlens_k)
     s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
-    _check(call_entry(params, batch, causal, varlen, tq, tk, s), "fmha_fwd")
+    if tiles is not None:
+        # device int32 [n, 2] work list (see fmha_native_b200.shard)
+        _check(call_tiles(params, batch, causal, tiles.data_ptr(), tiles.shape[0], tq, tk, s),
+               "fmha_fwd(tiles)")
+    else:
+        _check(call_entry(params, batch, causal, varlen, tq, tk, s), "fmha_fwd")
     return (o, lse) if return_lse else o

@@ -108,6 +108,7 @@ struct KernelArgs {
     unsigned long long wait_limit_ns;
     int stall_inject;          // test hook: producer withholds the first V tile
     unsigned long long* trace; // FMHA_TRACE builds: per-event clock64 of CTA (0,0)
+    const int32_t* tiles;      // optional work list of (b*nhead_q+h, query block)
 };
 
 // Pipeline event timestamps (diagnostic builds only, -DFMHA_TRACE): slot
@@ -179,13 +180,20 @@ struct TileWork {
 
 template <bool kCausal, bool kVarlen>
 __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
-    const int hb = blockIdx.x;
+    int hb, mblk;
+    if (a.tiles != nullptr) {
+        // Caller-supplied work list: (batch*nhead_q + head, query block).
+        hb = a.tiles[2 * blockIdx.x];
+        mblk = a.tiles[2 * blockIdx.x + 1];
+    } else {
+        hb = blockIdx.x;
+        // Causal work grows with the query block index, so launch the heavy
+        // blocks first (src/fused/kernel.cpp:73,96).
+        mblk = kCausal ? (int)(gridDim.y - 1 - blockIdx.y) : (int)blockIdx.y;
+    }
     w.h = hb % a.nhead_q;
     w.b = hb / a.nhead_q;
     w.kvh = w.h / (a.nhead_q / a.nhead_k);
-    // Causal work grows with the query block index, so launch the heavy
-    // blocks first (src/fused/kernel.cpp:73,96).
-    const int mblk = kCausal ? (int)(gridDim.y - 1 - blockIdx.y) : (int)blockIdx.y;
     if constexpr (kVarlen) {
         w.off_q = a.seqstart_q[w.b];
         w.off_k = a.seqstart_k[w.b];
@@ -770,7 +778,7 @@ bool stride_ok(long long s, int extent) {
 }
 
 int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
-           cudaStream_t stream) {
+           cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1) {
     if (p == nullptr || batch <= 0) return FMHA_ERR_ARG;
     if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
     if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
@@ -836,6 +844,11 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     const int m_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
     if (m_blocks > 65535) return FMHA_ERR_ARG;
     dim3 grid((unsigned)(p->nhead_q * batch), (unsigned)m_blocks, 1);
+    a.tiles = tiles;
+    if (tiles != nullptr) {
+        if (ntiles == 0) return FMHA_OK;
+        grid = dim3((unsigned)ntiles, 1, 1);
+    }
     dim3 block(kThreads);
     const size_t smem = kernel_smem_bytes<false, false>();
     if (causal) {
@@ -873,6 +886,16 @@ int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal, int to
     if (params == nullptr) return FMHA_ERR_ARG;
     const bool varlen = params->seqstart_q != nullptr;
     return launch(params, batch, causal != 0, varlen, total_q, total_k, stream);
+}
+
+int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal, int total_q,
+                            int total_k, const int32_t* tiles, int ntiles, CUstream_st* stream) {
+    if (params == nullptr || ntiles < 0) return FMHA_ERR_ARG;
+    if (ntiles == 0) return FMHA_OK;  // nothing to compute (tiles may be NULL)
+    if (tiles == nullptr) return FMHA_ERR_ARG;
+    if (((uintptr_t)tiles & 7u) != 0) return FMHA_ERR_ARG;
+    const bool varlen = params->seqstart_q != nullptr;
+    return launch(params, batch, causal != 0, varlen, total_q, total_k, stream, tiles, ntiles);
 }
 
 int fmha_fwd_d64_status(CUstream_st* stream) {

@@ -1,0 +1,83 @@
+"""Work partitioning of one forward pass across GPUs (and ordering within
+one GPU).
+
+The unit of work is a query block: 256 query rows (two 128-row tiles) of one
+(sequence, head), the work one CTA of the kernel performs.  Its cost is the
+number of 128-key tiles its two row tiles visit (causal blocks near the top
+of a sequence are cheap, blocks at the bottom are expensive) plus a fixed
+per-block overhead.  Blocks are independent -- each reads only its own Q rows
+and the K/V of its (sequence, kv head) -- so a partition needs no exchange:
+every rank holds K/V, runs `fmha_fwd_d64_bf16_tiles` on its own list and
+writes disjoint rows of O / LSE.
+
+`plan_blocks` lists the blocks with costs; `partition` assigns them to ranks
+with longest-processing-time-first greedy balancing, and returns each rank's
+list heavy-first (the in-GPU order that minimises the scheduling tail).
+"""
+from __future__ import annotations
+
+import heapq
+from typing import List, Optional, Sequence, Tuple
+
+ROWS_PER_BLOCK = 256
+ROWS_PER_TILE = 128
+KEYS_PER_TILE = 128
+BLOCK_OVERHEAD = 2.0  # per-block prologue/epilogue, in KV-tile units
+
+Block = Tuple[int, int, float]  # (b*nhead_q + h, query block index, cost)
+
+
+def _kv_tiles(r0: int, seqlen_q: int, seqlen_k: int, causal: bool) -> int:
+    if r0 >= seqlen_q:
+        return 0
+    kv_end = seqlen_k
+    if causal:
+        r_last = min(r0 + ROWS_PER_TILE - 1, seqlen_q - 1)
+        kv_end = min(seqlen_k, r_last + (seqlen_k - seqlen_q) + 1)
+    return (kv_end + KEYS_PER_TILE - 1) // KEYS_PER_TILE if kv_end > 0 else 0
+
+
+def block_cost(m: int, seqlen_q: int, seqlen_k: int, causal: bool) -> float:
+    r0 = m * ROWS_PER_BLOCK
+    n = (_kv_tiles(r0, seqlen_q, seqlen_k, causal) +
+         _kv_tiles(r0 + ROWS_PER_TILE, seqlen_q, seqlen_k, causal))
+    return float(n) + BLOCK_OVERHEAD
+
+
+def plan_blocks(batch: int, nhead_q: int, seqlen_q: int, seqlen_k: int, causal: bool,
+                varlen_seqs: Optional[Sequence[int]] = None) -> List[Block]:
+    """Every query block of the problem with its cost.  Varlen: sequence b
+    has Sq = Sk = varlen_seqs[b] (the reference's group-mode convention)."""
+    out: List[Block] = []
+    for b in range(batch):
+        sq = int(varlen_seqs[b]) if varlen_seqs else seqlen_q
+        sk = int(varlen_seqs[b]) if varlen_seqs else seqlen_k
+        nblk = (sq + ROWS_PER_BLOCK - 1) // ROWS_PER_BLOCK
+        for h in range(nhead_q):
+            for m in range(nblk):
+                out.append((b * nhead_q + h, m, block_cost(m, sq, sk, causal)))
+    return out
+
+
+def partition(blocks: Sequence[Block], world: int) -> List[List[Block]]:
+    """LPT greedy: blocks in decreasing cost go to the least-loaded rank.
+    Ties break on rank index, so every rank computes the same plan."""
+    order = sorted(blocks, key=lambda x: (-x[2], x[0], x[1]))
+    heap = [(0.0, r) for r in range(world)]
+    parts: List[List[Block]] = [[] for _ in range(world)]
+    for blk in order:
+        load, r = heapq.heappop(heap)
+        parts[r].append(blk)
+        heapq.heappush(heap, (load + blk[2], r))
+    return parts
+
+
+def loads(parts: Sequence[Sequence[Block]]) -> List[float]:
+    return [sum(b[2] for b in p) for p in parts]
+
+
+def tiles_array(part: Sequence[Block]):
+    """int32 [n, 2] array of (b*nhead_q + h, m) for the C ABI."""
+    import numpy as np
+
+    return np.asarray([(b[0], b[1]) for b in part], dtype=np.int32).reshape(-1, 2)

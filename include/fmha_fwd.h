@@ -112,6 +112,18 @@ int fmha_fwd_d64_bf16_msk1_varlen(const FmhaFwdParams* params, int batch,
 int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal,
                       int total_q, int total_k, struct CUstream_st* stream);
 
+/* Forward pass over an explicit list of query blocks: `tiles` is a device
+ * array of `ntiles` int32 pairs (b*nhead_q + h, m) naming the 256-row query
+ * block m of sequence b, head h.  Each listed block is computed exactly as
+ * by the entries above; blocks not listed are left untouched.  Used to shard
+ * one problem over several GPUs (every rank holds the full K/V and runs its
+ * own list, no collective) and to impose a load-balanced order.  Dense or
+ * varlen is selected as in fmha_fwd_d64_bf16.  No reference counterpart
+ * (the reference launches every block of the grid, src/fused/kernel.cpp). */
+int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal,
+                            int total_q, int total_k, const int32_t* tiles,
+                            int ntiles, struct CUstream_st* stream);
+
 /* Synchronizes `stream`, then reads and clears the device error word written
  * by bounded pipeline waits on the current device.  Returns FMHA_OK or
  * FMHA_ERR_TIMEOUT (or FMHA_ERR_LAUNCH if the synchronization failed).
@@ -134,6 +146,7 @@ const char* fmha_fwd_d64_error_string(int status);
  * launch geometry).  128 query rows per tile, two tiles per CTA, 128 keys per
  * KV tile. */
 #define FMHA_B200_BLOCK_M 128
+#define FMHA_B200_ROWS_PER_BLOCK 256 /* query rows per work-list entry */
 #define FMHA_B200_BLOCK_N 128
 #define FMHA_B200_HEAD_DIM 64
 
