@@ -202,7 +202,19 @@ def native_arm(args, workload_key):
     torch.cuda.set_device(dev)
     fm.load_library()
     w = WORKLOADS[workload_key]
-    q, k, v, cu = make_inputs(w, dev, seed_base=1000 * rank)
+    # Weak scaling (default): every rank runs its own copy of the workload on
+    # its own data.  --shard (strong scaling): one problem, every rank holds
+    # the same inputs and computes its share of the query blocks.
+    q, k, v, cu = make_inputs(w, dev, seed_base=0 if args.shard else 1000 * rank)
+    tiles = None
+    share = 1.0
+    if args.shard:
+        from fmha_native_b200 import shard as shd
+
+        blocks = shd.plan_blocks(w.batch, w.heads, w.seqlen, w.seqlen, w.causal, w.varlen_seqs)
+        part = shd.partition(blocks, world)[rank]
+        tiles = torch.from_numpy(shd.tiles_array(part)).to(dev)
+        share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
     layout = w.layout
     o = torch.empty_like(q)
     lse = None
@@ -217,7 +229,10 @@ def native_arm(args, workload_key):
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
 
     def step():
-        st = fm.call_entry(params, batch, w.causal, bool(w.varlen_seqs), tq, tk, sh)
+        if tiles is not None:
+            st = fm.call_tiles(params, batch, w.causal, tiles.data_ptr(), tiles.shape[0], tq, tk, sh)
+        else:
+            st = fm.call_entry(params, batch, w.causal, bool(w.varlen_seqs), tq, tk, sh)
         if st != fm.FMHA_OK:
             raise fm.FmhaError(st, "launch")
 
@@ -255,18 +270,19 @@ def native_arm(args, workload_key):
     if fm.status(sh) != fm.FMHA_OK:
         raise RuntimeError("device pipeline timeout during timed steps")
     ms_step = total_ms / args.steps
-    flops_rank = w.flops()
-    value = world * flops_rank / (ms_step * 1e-3) / 1e12
+    flops_rank = w.flops() * share
+    flops_job = w.flops() if args.shard else w.flops() * world
+    value = flops_job / (ms_step * 1e-3) / 1e12
     peak_tf, peak_hbm, peak_kind = load_peaks()
     achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API, copies inside the timed region
-    e2e = e2e_measure(fm, w, dev, args, params_builder=(layout, cu))
+    e2e = e2e_measure(fm, w, dev, args, tiles)
     if world > 1:
         t = torch.tensor([e2e["ms"]], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e["ms"] = float(t.item())
-    e2e_value = world * flops_rank / (e2e["ms"] * 1e-3) / 1e12
+    e2e_value = flops_job / (e2e["ms"] * 1e-3) / 1e12
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -278,12 +294,14 @@ def native_arm(args, workload_key):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": w.name, "per_gpu_batch": w.batch, "global_batch": w.batch * world,
+            "higher_is_better": True, "scaling": "strong" if args.shard else "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w.name, "per_gpu_batch": w.batch if not args.shard else None,
+                       "global_batch": w.batch if args.shard else w.batch * world,
                        "heads": w.heads, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
-                       "lse": w.lse, "parallelism": f"shard by (batch, head) over {world} GPU(s), "
-                       "K/V local, no collective", "l2": "flushed (256 MiB write) between steps"},
+                       "lse": w.lse, "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
+                                       "no collective" if args.shard else
+                                       f"{world} independent replicas (weak scaling), no collective"), "l2": "flushed (256 MiB write) between steps"},
             "pct_of_bf16_peak": round(100.0 * (value / world) / peak_tf, 2),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_tf,
                          "unit": UNIT, "frac": round(achieved / peak_tf, 4),
@@ -303,7 +321,7 @@ def native_arm(args, workload_key):
     return 0
 
 
-def e2e_measure(fm, w, dev, args, params_builder):
+def e2e_measure(fm, w, dev, args, tiles=None):
     """Public API with pinned host buffers: H2D of Q,K,V (and cu_seqlens),
     the kernel, D2H of O (and LSE) -- all inside CUDA events."""
     import torch
@@ -314,6 +332,7 @@ def e2e_measure(fm, w, dev, args, params_builder):
     hcu = cu.cpu().pin_memory() if cu is not None else None
     ho = torch.empty_like(hq).pin_memory()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    do = torch.zeros_like(q)
     dcu = torch.empty_like(cu) if cu is not None else None
     hl = None
     stream = torch.cuda.current_stream(dev)
@@ -327,7 +346,8 @@ def e2e_measure(fm, w, dev, args, params_builder):
         if dcu is not None:
             dcu.copy_(hcu, non_blocking=True)
         o = fm.fmha_fwd(dq, dk, dv, causal=w.causal, return_lse=False, layout=w.layout,
-                        cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream)
+                        cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream,
+                        out=do, tiles=tiles)
         ho.copy_(o, non_blocking=True)
 
     for _ in range(2):
@@ -371,6 +391,8 @@ def main():
     ap.add_argument("--config", default="c2")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", action="store_true",
+                    help="strong scaling: split one problem's query blocks over the ranks")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch to report in roofline.traffic")
     args = ap.parse_args()
