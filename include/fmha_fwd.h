@@ -24,7 +24,8 @@
  *   r = nhead_q / nhead_k (GQA/MQA).  Causal ("msk1") is bottom-right aligned:
  *   query i attends key j iff j <= i + (seqlen_k - seqlen_q).  Rows with no
  *   visible key produce O = 0 and LSE = -inf.  P is truncated to bf16 before the
- *   P.V product and O is truncated to bf16, as in the reference kernel.
+ *   P.V product, as in the reference kernel; O is rounded to nearest-even bf16
+ *   (the reference truncates; build with -DFMHA_O_ROUND_TRUNC for that).
  *   LSE (natural log, fp32) is written when params->lse != NULL:
  *     dense : lse[(b*nhead_q + h)*seqlen_q + i]
  *     varlen: lse[h*total_q + seqstart_q[b] + i]
