@@ -38,6 +38,7 @@ FMHA_ERR_ARG = 1
 FMHA_ERR_LAUNCH = 2
 FMHA_ERR_TIMEOUT = 3
 FMHA_ERR_DEVICE = 4
+FMHA_ERR_SCRATCH = 5
 
 ENTRY_POINTS = (
     "fmha_fwd_d64_bf16_msk0",
@@ -122,7 +123,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
 
 def error_string(status: int) -> str:
     names = {0: "ok", 1: "invalid argument", 2: "CUDA launch or runtime error",
-             3: "device pipeline wait exceeded its time limit", 4: "no supported sm_100 device"}
+             3: "device pipeline wait exceeded its time limit", 4: "no supported sm_100 device",
+             5: "request exceeds the allocation-free scratch"}
     return names.get(status, "unknown status")
 
 

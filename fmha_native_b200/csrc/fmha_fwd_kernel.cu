@@ -863,6 +863,171 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
 
 }  // namespace
 
+// ============================================ allocation-free variant (host)
+//
+// For callers that may not allocate device memory themselves -- for example
+// code that runs where a cudaMalloc would be refused or would stall the whole
+// device (inside a stream capture, or a serving loop that must never
+// synchronise), or a plug-in whose host framework owns every allocation.  The
+// regular entries allocate a small per-device error word on their first call;
+// this variant instead keeps its scratch (the error word and a staged copy of
+// the caller's work list) in the file-scope array below, which every GPU that
+// loads the library holds until the process exits.
+namespace {
+
+constexpr int kNoAllocMaxTiles = 16384;     // work-list capacity (query blocks)
+constexpr int kNoAllocHeaderInts = 64;      // [0] = device error word
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocHeaderInts + 2 * kNoAllocMaxTiles];
+
+struct NoAllocDevice {
+    bool ready = false;
+    int32_t* scratch = nullptr;  // device address of g_noalloc_scratch on that device
+};
+std::vector<NoAllocDevice> g_noalloc;
+
+// Once per device, with that device current: resolve the device address of
+// the scratch array (the host-side name is only a stand-in) and set the
+// kernels' shared-memory attribute.  Allocates nothing.
+int noalloc_setup(int dev, int32_t** scratch) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_encode == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            fn == nullptr)
+            return FMHA_ERR_DEVICE;
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if ((int)g_noalloc.size() <= dev) g_noalloc.resize(dev + 1);
+    NoAllocDevice& d = g_noalloc[dev];
+    if (!d.ready) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+        if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+            return FMHA_ERR_LAUNCH;
+        const int smem = (int)kernel_smem_bytes<false, false>();
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
+        d.scratch = static_cast<int32_t*>(ptr);
+        d.ready = true;
+    }
+    *scratch = d.scratch;
+    return FMHA_OK;
+}
+
+int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, int total_k,
+                   const int32_t* host_tiles, int ntiles, cudaStream_t stream) {
+    if (p == nullptr || batch <= 0 || ntiles < 0) return FMHA_ERR_ARG;
+    if (ntiles > kNoAllocMaxTiles) return FMHA_ERR_SCRATCH;
+    if (ntiles > 0 && host_tiles == nullptr) return FMHA_ERR_ARG;
+    const bool varlen = p->seqstart_q != nullptr;
+    if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
+    if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
+    if (p->seqlen_q < 0 || p->seqlen_k < 0) return FMHA_ERR_ARG;
+    if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
+        return FMHA_ERR_ARG;
+    if (varlen && (!p->seqstart_k || total_q < 0 || total_k < 0)) return FMHA_ERR_ARG;
+    const int rows_q = varlen ? total_q : p->seqlen_q;
+    const int rows_k = varlen ? total_k : p->seqlen_k;
+    if (!stride_ok(p->stride_q, rows_q) || !stride_ok(p->stride_k, rows_k) ||
+        !stride_ok(p->stride_v, rows_k) || !stride_ok(p->nhead_stride_q, p->nhead_q) ||
+        !stride_ok(p->nhead_stride_k, p->nhead_k) || !stride_ok(p->nhead_stride_v, p->nhead_k))
+        return FMHA_ERR_ARG;
+    if (!varlen && (!stride_ok(p->batch_stride_q, batch) || !stride_ok(p->batch_stride_k, batch) ||
+                    !stride_ok(p->batch_stride_v, batch)))
+        return FMHA_ERR_ARG;
+    if ((p->stride_o % 8) != 0 || (p->nhead_stride_o % 8) != 0 ||
+        (!varlen && (p->batch_stride_o % 8) != 0))
+        return FMHA_ERR_ARG;
+    if (ntiles == 0 || p->seqlen_q == 0 || rows_q == 0) return FMHA_OK;
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    int32_t* scratch = nullptr;
+    int st = noalloc_setup(dev, &scratch);
+    if (st != FMHA_OK) return st;
+
+    KernelArgs a;
+    memset(&a, 0, sizeof(a));
+    const int rank = varlen ? 3 : 4;
+    const int mb = varlen ? 1 : batch;
+    const int rk = rows_k > 0 ? rows_k : 1;
+    if ((st = make_map(&a.tm_q, p->q, rank, rows_q, p->nhead_q, mb, p->stride_q,
+                       p->nhead_stride_q, p->batch_stride_q)) != FMHA_OK)
+        return st;
+    if ((st = make_map(&a.tm_k, p->k, rank, rk, p->nhead_k, mb, p->stride_k, p->nhead_stride_k,
+                       p->batch_stride_k)) != FMHA_OK)
+        return st;
+    if ((st = make_map(&a.tm_v, p->v, rank, rk, p->nhead_k, mb, p->stride_v, p->nhead_stride_v,
+                       p->batch_stride_v)) != FMHA_OK)
+        return st;
+    a.o = p->o;
+    a.lse = p->lse;
+    a.seqstart_q = p->seqstart_q;
+    a.seqstart_k = p->seqstart_k;
+    a.stride_o = p->stride_o;
+    a.nhead_stride_o = p->nhead_stride_o;
+    a.batch_stride_o = p->batch_stride_o;
+    a.seqlen_q = p->seqlen_q;
+    a.seqlen_k = p->seqlen_k;
+    a.nhead_q = p->nhead_q;
+    a.nhead_k = p->nhead_k;
+    a.total_q = total_q;
+    a.scale = p->scale;
+    a.err_word = scratch;  // header word 0
+    a.wait_limit_ns = g_wait_limit_ns;
+    a.stall_inject = 0;
+    a.trace = nullptr;
+    a.tiles = scratch + kNoAllocHeaderInts;
+
+    // The array keeps the previous call's contents: clear the error word and
+    // stage this call's work list, in stream order before the kernel.
+    if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), stream) != cudaSuccess) return FMHA_ERR_LAUNCH;
+    if (cudaMemcpyAsync(scratch + kNoAllocHeaderInts, host_tiles,
+                        sizeof(int32_t) * 2 * (size_t)ntiles, cudaMemcpyHostToDevice,
+                        stream) != cudaSuccess)
+        return FMHA_ERR_LAUNCH;
+    dim3 grid((unsigned)ntiles, 1, 1);
+    dim3 block(kThreads);
+    const size_t smem = kernel_smem_bytes<false, false>();
+    if (causal) {
+        if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, smem, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<true, false><<<grid, block, smem, stream>>>(a);
+    } else {
+        if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
+    }
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
+}
+
+int noalloc_status(cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return FMHA_ERR_LAUNCH;
+    int32_t* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if (dev < (int)g_noalloc.size() && g_noalloc[dev].ready) scratch = g_noalloc[dev].scratch;
+    }
+    if (scratch == nullptr) return FMHA_OK;
+    int h = 0;
+    if (cudaMemcpy(&h, scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return FMHA_ERR_LAUNCH;
+    return h != 0 ? FMHA_ERR_TIMEOUT : FMHA_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 int fmha_fwd_d64_bf16_msk0(const FmhaFwdParams* params, int batch, CUstream_st* stream) {
@@ -952,6 +1117,15 @@ void fmha_fwd_d64_release(void) {
     cudaSetDevice(cur);
 }
 
+int fmha_fwd_d64_bf16_tiles_noalloc(const FmhaFwdParams* params, int batch, int causal,
+                                    int total_q, int total_k, const int32_t* host_tiles,
+                                    int ntiles, CUstream_st* stream) {
+    return launch_noalloc(params, batch, causal != 0, total_q, total_k, host_tiles, ntiles,
+                          stream);
+}
+
+int fmha_fwd_d64_noalloc_status(CUstream_st* stream) { return noalloc_status(stream); }
+
 const char* fmha_fwd_d64_error_string(int status) {
     switch (status) {
         case FMHA_OK: return "ok";
@@ -959,6 +1133,8 @@ const char* fmha_fwd_d64_error_string(int status) {
         case FMHA_ERR_LAUNCH: return "CUDA launch or runtime error";
         case FMHA_ERR_TIMEOUT: return "device pipeline wait exceeded its time limit";
         case FMHA_ERR_DEVICE: return "no supported sm_100 device";
+        case FMHA_ERR_SCRATCH:
+            return "work list longer than the allocation-free entry's scratch (16384 blocks)";
         default: return "unknown status";
     }
 }

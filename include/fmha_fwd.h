@@ -80,7 +80,8 @@ enum {
     FMHA_ERR_ARG = 1,      /* invalid argument (see restrictions above)       */
     FMHA_ERR_LAUNCH = 2,   /* CUDA launch / driver error                       */
     FMHA_ERR_TIMEOUT = 3,  /* a device-side pipeline wait exceeded its limit   */
-    FMHA_ERR_DEVICE = 4    /* no sm_100 device / unsupported device            */
+    FMHA_ERR_DEVICE = 4,   /* no sm_100 device / unsupported device            */
+    FMHA_ERR_SCRATCH = 5   /* request exceeds the allocation-free scratch      */
 };
 
 /* Dense (fixed-length batch) forward, no mask.
@@ -124,6 +125,32 @@ int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal,
 int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal,
                             int total_q, int total_k, const int32_t* tiles,
                             int ntiles, struct CUstream_st* stream);
+
+/* Allocation-free variant of fmha_fwd_d64_bf16_tiles.  No counterpart in the
+ * reference.  Meant for callers that may not allocate device memory: code
+ * running where cudaMalloc is refused or would stall the device (inside a
+ * stream capture, a serving loop that must never synchronise) or a plug-in
+ * whose host framework owns all allocations.  The regular entries allocate a
+ * 4-byte error word per device on first use; this one allocates nothing and
+ * keeps its scratch -- the error word and a copy of the work list -- in a
+ * fixed 128 KB array inside the library (held by every GPU that loads it).
+ *   host_tiles : HOST array of ntiles int32 pairs (b*nhead_q + h, m), as for
+ *                fmha_fwd_d64_bf16_tiles; copied in stream order, so it may
+ *                be reused once the call returns.
+ *   ntiles     : at most 16384, else FMHA_ERR_SCRATCH and nothing is launched.
+ * The first call on a device resolves the scratch address for that device
+ * (make it before any stream capture begins).  All calls share the one array
+ * and each call overwrites it: calls whose executions overlap on the GPU race
+ * and must be serialised (e.g. one stream).  Read device timeouts with
+ * fmha_fwd_d64_noalloc_status. */
+int fmha_fwd_d64_bf16_tiles_noalloc(const FmhaFwdParams* params, int batch, int causal,
+                                    int total_q, int total_k, const int32_t* host_tiles,
+                                    int ntiles, struct CUstream_st* stream);
+
+/* Synchronizes `stream` and reports FMHA_ERR_TIMEOUT if the last
+ * allocation-free call's pipeline waits expired (FMHA_OK otherwise).  No
+ * counterpart in the reference. */
+int fmha_fwd_d64_noalloc_status(struct CUstream_st* stream);
 
 /* Synchronizes `stream`, then reads and clears the device error word written
  * by bounded pipeline waits on the current device.  Returns FMHA_OK or
