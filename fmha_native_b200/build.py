@@ -60,6 +60,24 @@ def build_library(force: bool = False, verbose: bool = False, extra_flags: list[
     return LIB_PATH
 
 
+CLI_SRC = os.path.join(PKG_DIR, "host", "bench_fmha_fwd.cpp")
+CLI_PATH = os.path.join(PKG_DIR, "bench_fmha_fwd")
+
+
+def build_cli(force: bool = False) -> str:
+    """C++17 bench_fmha_fwd CLI over the C ABI (links libfmha_b200.so)."""
+    lib = build_library()
+    if not force and not _stale(CLI_PATH, [CLI_SRC, lib, os.path.join(REPO_DIR, "include", "fmha_fwd.h")]):
+        return CLI_PATH
+    cuda = os.path.dirname(os.path.dirname(nvcc_path()))
+    subprocess.run(["g++", "-std=c++17", "-O2", "-I", os.path.join(REPO_DIR, "include"),
+                    "-I", os.path.join(cuda, "include"), CLI_SRC, "-o", CLI_PATH,
+                    "-L", PKG_DIR, "-lfmha_b200", f"-Wl,-rpath,$ORIGIN",
+                    "-L", os.path.join(cuda, "lib64"), "-lcudart"], check=True)
+    return CLI_PATH
+
+
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    build_cli(force="--force" in sys.argv)
     print(LIB_PATH)
