@@ -215,6 +215,14 @@ def native_arm(args, workload_key):
         part = shd.partition(blocks, world)[rank]
         tiles = torch.from_numpy(shd.tiles_array(part)).to(dev)
         share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
+    splits = 1
+    workspace = None
+    if tiles is not None:
+        # split-KV when this rank's blocks cannot fill the GPU (long causal, few heads)
+        splits = args.splits if args.splits > 0 else shd.choose_splits(tiles.shape[0])
+        if splits > 1:
+            workspace = torch.empty(fm.splitkv_workspace_bytes(tiles.shape[0], splits) // 4,
+                                    device=dev, dtype=torch.float32)
     layout = w.layout
     o = torch.empty_like(q)
     lse = None
@@ -229,7 +237,10 @@ def native_arm(args, workload_key):
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
 
     def step():
-        if tiles is not None:
+        if tiles is not None and splits > 1:
+            st = fm.call_tiles_splitkv(params, batch, w.causal, tiles.data_ptr(), tiles.shape[0],
+                                       splits, workspace.data_ptr(), workspace.numel() * 4, tq, tk, sh)
+        elif tiles is not None:
             st = fm.call_tiles(params, batch, w.causal, tiles.data_ptr(), tiles.shape[0], tq, tk, sh)
         else:
             st = fm.call_entry(params, batch, w.causal, bool(w.varlen_seqs), tq, tk, sh)
@@ -277,7 +288,7 @@ def native_arm(args, workload_key):
     achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API, copies inside the timed region
-    e2e = e2e_measure(fm, w, dev, args, tiles)
+    e2e = e2e_measure(fm, w, dev, args, tiles, splits)
     if world > 1:
         t = torch.tensor([e2e["ms"]], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -299,7 +310,7 @@ def native_arm(args, workload_key):
             "config": {"workload": w.name, "per_gpu_batch": w.batch if not args.shard else None,
                        "global_batch": w.batch if args.shard else w.batch * world,
                        "heads": w.heads, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
-                       "lse": w.lse, "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
+                       "lse": w.lse, "splitkv": splits, "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
                                        "no collective" if args.shard else
                                        f"{world} independent replicas (weak scaling), no collective"), "l2": "flushed (256 MiB write) between steps"},
             "pct_of_bf16_peak": round(100.0 * (value / world) / peak_tf, 2),
@@ -321,7 +332,7 @@ def native_arm(args, workload_key):
     return 0
 
 
-def e2e_measure(fm, w, dev, args, tiles=None):
+def e2e_measure(fm, w, dev, args, tiles=None, splits=1):
     """Public API with pinned host buffers: H2D of Q,K,V (and cu_seqlens),
     the kernel, D2H of O (and LSE) -- all inside CUDA events."""
     import torch
@@ -347,7 +358,7 @@ def e2e_measure(fm, w, dev, args, tiles=None):
             dcu.copy_(hcu, non_blocking=True)
         o = fm.fmha_fwd(dq, dk, dv, causal=w.causal, return_lse=False, layout=w.layout,
                         cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream,
-                        out=do, tiles=tiles)
+                        out=do, tiles=tiles, num_splits=splits)
         ho.copy_(o, non_blocking=True)
 
     for _ in range(2):
@@ -391,6 +402,8 @@ def main():
     ap.add_argument("--config", default="c2")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="split-KV factor for --shard (0 = automatic)")
     ap.add_argument("--shard", action="store_true",
                     help="strong scaling: split one problem's query blocks over the ranks")
     ap.add_argument("--traffic", type=float, default=None,

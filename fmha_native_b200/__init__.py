@@ -47,6 +47,8 @@ ENTRY_POINTS = (
     "fmha_fwd_d64_bf16_msk1_varlen",
     "fmha_fwd_d64_bf16",
     "fmha_fwd_d64_bf16_tiles",
+    "fmha_fwd_d64_bf16_tiles_splitkv",
+    "fmha_fwd_d64_splitkv_workspace_bytes",
     "fmha_fwd_d64_status",
     "fmha_fwd_d64_set_wait_limit_ns",
     "fmha_fwd_d64_release",
@@ -107,6 +109,13 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
                                             ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                             ctypes.c_void_p]
     lib.fmha_fwd_d64_bf16_tiles.restype = ctypes.c_int
+    lib.fmha_fwd_d64_bf16_tiles_splitkv.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                                    ctypes.c_void_p]
+    lib.fmha_fwd_d64_bf16_tiles_splitkv.restype = ctypes.c_int
+    lib.fmha_fwd_d64_splitkv_workspace_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
+    lib.fmha_fwd_d64_splitkv_workspace_bytes.restype = ctypes.c_size_t
     lib.fmha_fwd_d64_status.argtypes = [ctypes.c_void_p]
     lib.fmha_fwd_d64_status.restype = ctypes.c_int
     lib.fmha_fwd_d64_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
@@ -195,6 +204,21 @@ def call_tiles(params: FmhaFwdParams, batch: int, causal: bool, tiles_ptr: int, 
                                        ctypes.c_void_p(tiles_ptr), ntiles, ctypes.c_void_p(stream))
 
 
+def splitkv_workspace_bytes(ntiles: int, num_splits: int) -> int:
+    return int(load_library().fmha_fwd_d64_splitkv_workspace_bytes(ntiles, num_splits))
+
+
+def call_tiles_splitkv(params: FmhaFwdParams, batch: int, causal: bool, tiles_ptr: int,
+                       ntiles: int, num_splits: int, workspace_ptr: int, workspace_bytes: int,
+                       total_q: int = 0, total_k: int = 0, stream: int = 0) -> int:
+    """Call fmha_fwd_d64_bf16_tiles_splitkv (split-KV over a device work list)."""
+    lib = load_library()
+    return lib.fmha_fwd_d64_bf16_tiles_splitkv(
+        ctypes.byref(params), batch, int(causal), total_q, total_k, ctypes.c_void_p(tiles_ptr),
+        ntiles, num_splits, ctypes.c_void_p(workspace_ptr), workspace_bytes,
+        ctypes.c_void_p(stream))
+
+
 def status(stream: int = 0) -> int:
     """Synchronise `stream` and read/clear the device error word."""
     return load_library().fmha_fwd_d64_status(ctypes.c_void_p(stream))
@@ -247,7 +271,7 @@ def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
 
 def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: str = "bshd",
              cu_seqlens_q=None, cu_seqlens_k=None, out=None, lse_out=None, stream=None,
-             tiles=None):
+             tiles=None, num_splits: int = 1, workspace=None):
     """O = softmax(Q K^T / 8) V on the B200 kernel (head_dim 64, bf16).
 
     Dense: q [B,Sq,Hq,64] ("bshd") or [B,Hq,Sq,64] ("bhsd"); varlen: q
@@ -255,6 +279,9 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
     Returns O (and fp32 LSE [B,Hq,Sq] / [Hq,total] when return_lse).
     `tiles`: optional device int32 [n, 2] list of query blocks to compute
     (fmha_native_b200.shard); other rows of `out` are left untouched.
+    `num_splits` > 1 (with `tiles`) splits each block's key range (split-KV);
+    `workspace` is then a device buffer of splitkv_workspace_bytes() bytes
+    (allocated here when omitted).
     """
     import torch
 
@@ -277,7 +304,15 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
                               dtype=torch.float32)
     params, batch, tq, tk = params_from_tensors(q, k, v, o, lse, layout, cu_seqlens_q, cu_seqlens_k)
     s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
-    if tiles is not None:
+    if tiles is not None and num_splits > 1:
+        nbytes = splitkv_workspace_bytes(tiles.shape[0], num_splits)
+        if workspace is None:
+            workspace = torch.empty(nbytes // 4, device=q.device, dtype=torch.float32)
+        _check(call_tiles_splitkv(params, batch, causal, tiles.data_ptr(), tiles.shape[0],
+                                  num_splits, workspace.data_ptr(),
+                                  workspace.numel() * workspace.element_size(), tq, tk, s),
+               "fmha_fwd(split-KV)")
+    elif tiles is not None:
         # device int32 [n, 2] work list (see fmha_native_b200.shard)
         _check(call_tiles(params, batch, causal, tiles.data_ptr(), tiles.shape[0], tq, tk, s),
                "fmha_fwd(tiles)")

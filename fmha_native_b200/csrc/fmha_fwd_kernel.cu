@@ -109,6 +109,9 @@ struct KernelArgs {
     int stall_inject;          // test hook: producer withholds the first V tile
     unsigned long long* trace; // FMHA_TRACE builds: per-event clock64 of CTA (0,0)
     const int32_t* tiles;      // optional work list of (b*nhead_q+h, query block)
+    int num_splits;            // split-KV: work item x = (tiles[x / num_splits], KV range x % num_splits)
+    float* part_o;             // split-KV partial O (fp32, normalised) [item][256][64]
+    float* part_lse;           // split-KV partial LSE (natural log) [item][256]
 };
 
 // Pipeline event timestamps (diagnostic builds only, -DFMHA_TRACE): slot
@@ -171,7 +174,8 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const
 }
 
 struct TileWork {
-    int n_kv[kTilesPerCta];     // KV tiles each query tile walks
+    int n_kv[kTilesPerCta];     // KV tiles each query tile walks (from j0)
+    int j0;                     // first KV tile (split-KV ranges start past 0)
     int row0;                   // first query row of the CTA (sequence-local)
     int seqlen_q, seqlen_k;
     int off_q, off_k;           // varlen packed-row offsets
@@ -181,10 +185,14 @@ struct TileWork {
 template <bool kCausal, bool kVarlen>
 __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
     int hb, mblk;
+    int split = 0;
     if (a.tiles != nullptr) {
-        // Caller-supplied work list: (batch*nhead_q + head, query block).
-        hb = a.tiles[2 * blockIdx.x];
-        mblk = a.tiles[2 * blockIdx.x + 1];
+        // Caller-supplied work list: (batch*nhead_q + head, query block); in
+        // split-KV mode every entry expands into num_splits KV ranges.
+        const int x = a.num_splits > 1 ? (int)blockIdx.x / a.num_splits : (int)blockIdx.x;
+        if (a.num_splits > 1) split = (int)blockIdx.x % a.num_splits;
+        hb = a.tiles[2 * x];
+        mblk = a.tiles[2 * x + 1];
     } else {
         hb = blockIdx.x;
         // Causal work grows with the query block index, so launch the heavy
@@ -221,6 +229,17 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
             kv_end = min(w.seqlen_k, r_last + shift + 1);
         }
         w.n_kv[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+    }
+    w.j0 = 0;
+    if (a.num_splits > 1) {
+        // KV range of this split: an equal share of the longer tile's range.
+        const int n_all = max(w.n_kv[0], w.n_kv[1]);
+        const int chunk = (n_all + a.num_splits - 1) / a.num_splits;
+        const int jb = split * chunk;
+        const int je = min(n_all, jb + chunk);
+        w.j0 = jb;
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], je) - jb);
     }
     return true;
 }
@@ -325,7 +344,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 mbar_arrive_expect_tx(bar, kTileBytes);
                 const CUtensorMap* tm = (idx & 1) ? &a.tm_v : &a.tm_k;
                 tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), tm, bar,
-                                       w.off_k + (idx >> 1) * kBlockN, w.kvh,
+                                       w.off_k + (w.j0 + (idx >> 1)) * kBlockN, w.kvh,
                                        kVarlen ? 0 : w.b, pol_kv);
                 issued = idx + 1;
             }
@@ -500,7 +519,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             mbar_arrive(smem_u32(&sm.bar_sfree[i]));
             if (t == 0) TRACE_EV(i, j, 2);
 
-            const int k0 = j * kBlockN;
+            const int k0 = (w.j0 + j) * kBlockN;
             const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
                                    (kCausal && k0 + kBlockN - 1 > tile_row0 + shift);
             if (need_mask) {
@@ -642,7 +661,27 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 reg_fence(o[0]);
                 reg_fence(o[1]);
             }
-            if (row < w.seqlen_q) {
+            if (a.part_o != nullptr) {
+                // Split-KV: this item's normalised partial O (fp32) and LSE;
+                // the combine kernel merges the splits of each query block.
+                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+                const size_t prow = (size_t)blockIdx.x * kRowsPerCta + (size_t)i * kBlockM + t;
+                float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    float v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = c * 4 + e;
+                        v[e] = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
+                    }
+                    dst[c] = make_float4(v[0], v[1], v[2], v[3]);
+                }
+                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                a.part_lse[prow] = (l_run > 0.0f)
+                                       ? (__log2f(l_run) + m_use * scale) * 0.69314718055994531f
+                                       : -INFINITY;
+            } else if (row < w.seqlen_q) {
                 const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
                 uint16_t* orow;
                 if constexpr (kVarlen) {
@@ -692,6 +731,83 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     if (warp == kWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+
+// Split-KV combine: one thread per query row of every listed block.
+// LSE = log(sum_s exp(lse_s)); O = sum_s exp(lse_s - LSE) * O_s, rounded to
+// bf16 like the main epilogue; the same LSE merge the reference's base-2
+// epilogue formula implies (src/fused/op_epilog.hpp:92-98).
+template <bool kVarlen>
+__global__ void __launch_bounds__(128)
+fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
+    const int item_block = blockIdx.x / 2;          // 2 x 128 rows per block
+    const int r = (blockIdx.x & 1) * 128 + threadIdx.x;
+    if (item_block >= nblocks) return;
+    const int hb = a.tiles[2 * item_block];
+    const int mblk = a.tiles[2 * item_block + 1];
+    const int h = hb % a.nhead_q, b = hb / a.nhead_q;
+    int seqlen_q = a.seqlen_q, off_q = 0;
+    if constexpr (kVarlen) {
+        off_q = a.seqstart_q[b];
+        seqlen_q = a.seqstart_q[b + 1] - off_q;
+    }
+    const int row = mblk * kRowsPerCta + r;
+    if (row >= seqlen_q) return;
+    const int S = a.num_splits;
+    float mx = -INFINITY;
+    for (int s = 0; s < S; ++s)
+        mx = fmaxf(mx, a.part_lse[(size_t)(item_block * S + s) * kRowsPerCta + r]);
+    float acc[kHeadDim];
+#pragma unroll
+    for (int d = 0; d < kHeadDim; ++d) acc[d] = 0.0f;
+    float wsum = 0.0f;
+    if (mx != -INFINITY) {
+        for (int s = 0; s < S; ++s) {
+            const size_t prow = (size_t)(item_block * S + s) * kRowsPerCta + r;
+            const float l = a.part_lse[prow];
+            if (l == -INFINITY) continue;
+            const float wgt = __expf(l - mx);
+            wsum += wgt;
+            const float4* src = reinterpret_cast<const float4*>(a.part_o + prow * kHeadDim);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const float4 v = src[c];
+                acc[4 * c] += wgt * v.x;
+                acc[4 * c + 1] += wgt * v.y;
+                acc[4 * c + 2] += wgt * v.z;
+                acc[4 * c + 3] += wgt * v.w;
+            }
+        }
+    }
+    const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+    uint16_t* orow;
+    if constexpr (kVarlen) {
+        orow = a.o + (long long)h * a.nhead_stride_o + (long long)(off_q + row) * a.stride_o;
+    } else {
+        orow = a.o + (long long)b * a.batch_stride_o + (long long)h * a.nhead_stride_o +
+               (long long)row * a.stride_o;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+#ifdef FMHA_O_ROUND_TRUNC
+            pk[e] = pack_bf16_trunc(acc[c * 8 + 2 * e] * inv, acc[c * 8 + 2 * e + 1] * inv);
+#else
+            pk[e] = pack_bf16_rne(acc[c * 8 + 2 * e] * inv, acc[c * 8 + 2 * e + 1] * inv);
+#endif
+        }
+        dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    if (a.lse != nullptr) {
+        const float lse = wsum > 0.0f ? mx + __logf(wsum) : -INFINITY;
+        const long long idx = kVarlen ? (long long)h * a.total_q + off_q + row
+                                      : ((long long)b * a.nhead_q + h) * a.seqlen_q + row;
+        a.lse[idx] = lse;
     }
 }
 
@@ -778,7 +894,8 @@ bool stride_ok(long long s, int extent) {
 }
 
 int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
-           cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1) {
+           cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1,
+           int num_splits = 1, float* workspace = nullptr) {
     if (p == nullptr || batch <= 0) return FMHA_ERR_ARG;
     if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
     if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
@@ -845,9 +962,16 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     if (m_blocks > 65535) return FMHA_ERR_ARG;
     dim3 grid((unsigned)(p->nhead_q * batch), (unsigned)m_blocks, 1);
     a.tiles = tiles;
+    a.num_splits = 1;
     if (tiles != nullptr) {
         if (ntiles == 0) return FMHA_OK;
         grid = dim3((unsigned)ntiles, 1, 1);
+        if (num_splits > 1) {
+            a.num_splits = num_splits;
+            a.part_o = workspace;
+            a.part_lse = workspace + (size_t)ntiles * num_splits * kRowsPerCta * kHeadDim;
+            grid = dim3((unsigned)(ntiles * num_splits), 1, 1);
+        }
     }
     dim3 block(kThreads);
     const size_t smem = kernel_smem_bytes<false, false>();
@@ -857,6 +981,12 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     } else {
         if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
         else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
+    }
+    if (a.num_splits > 1) {
+        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
+        dim3 cgrid((unsigned)(2 * ntiles), 1, 1);
+        if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, 128, 0, stream>>>(a, ntiles);
+        else fmha_fwd_d64_splitkv_combine<false><<<cgrid, 128, 0, stream>>>(a, ntiles);
     }
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
 }
@@ -1061,6 +1191,29 @@ int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal, 
     if (((uintptr_t)tiles & 7u) != 0) return FMHA_ERR_ARG;
     const bool varlen = params->seqstart_q != nullptr;
     return launch(params, batch, causal != 0, varlen, total_q, total_k, stream, tiles, ntiles);
+}
+
+size_t fmha_fwd_d64_splitkv_workspace_bytes(int ntiles, int num_splits) {
+    if (ntiles <= 0 || num_splits <= 0) return 0;
+    return (size_t)ntiles * num_splits * kRowsPerCta * (kHeadDim + 1) * sizeof(float);
+}
+
+int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int causal,
+                                    int total_q, int total_k, const int32_t* tiles, int ntiles,
+                                    int num_splits, void* workspace, size_t workspace_bytes,
+                                    CUstream_st* stream) {
+    if (params == nullptr || ntiles < 0 || num_splits < 1 || num_splits > 64) return FMHA_ERR_ARG;
+    if (ntiles == 0) return FMHA_OK;
+    if (tiles == nullptr || ((uintptr_t)tiles & 7u) != 0) return FMHA_ERR_ARG;
+    if (num_splits == 1)
+        return launch(params, batch, causal != 0, params->seqstart_q != nullptr, total_q, total_k,
+                      stream, tiles, ntiles);
+    if (workspace == nullptr || ((uintptr_t)workspace & 15u) != 0 ||
+        workspace_bytes < fmha_fwd_d64_splitkv_workspace_bytes(ntiles, num_splits))
+        return FMHA_ERR_ARG;
+    if ((long long)ntiles * num_splits > 0x7fffffffll) return FMHA_ERR_ARG;
+    return launch(params, batch, causal != 0, params->seqstart_q != nullptr, total_q, total_k,
+                  stream, tiles, ntiles, num_splits, static_cast<float*>(workspace));
 }
 
 int fmha_fwd_d64_status(CUstream_st* stream) {

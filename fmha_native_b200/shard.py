@@ -81,3 +81,13 @@ def tiles_array(part: Sequence[Block]):
     import numpy as np
 
     return np.asarray([(b[0], b[1]) for b in part], dtype=np.int32).reshape(-1, 2)
+
+
+def choose_splits(nblocks: int, sms: int = 148, target_waves: float = 2.0,
+                  max_splits: int = 8) -> int:
+    """Split-KV factor so that a launch of `nblocks` query blocks still has
+    about `target_waves` work items per SM (1 when the blocks already do)."""
+    if nblocks <= 0:
+        return 1
+    want = int(-(-target_waves * sms // nblocks))
+    return max(1, min(max_splits, want))

@@ -41,6 +41,7 @@
 #ifndef FMHA_FWD_H_
 #define FMHA_FWD_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -125,6 +126,24 @@ int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal,
 int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal,
                             int total_q, int total_k, const int32_t* tiles,
                             int ntiles, struct CUstream_st* stream);
+
+/* Split-KV variant of fmha_fwd_d64_bf16_tiles for problems with too few query
+ * blocks to fill the GPU (long sequences with few heads, or one rank's shard
+ * of such a problem).  Every listed query block is computed as num_splits
+ * independent work items over equal shares of its key range; each writes a
+ * normalised fp32 partial O and its log-sum-exp into `workspace` (device
+ * memory of at least fmha_fwd_d64_splitkv_workspace_bytes(ntiles, num_splits)
+ * bytes, 16-byte aligned, owned by the caller), and a second kernel on the
+ * same stream merges them: LSE = log sum_s exp(lse_s), O = sum_s
+ * exp(lse_s - LSE) O_s.  Results equal the one-pass kernel up to fp32
+ * rounding.  num_splits in [1, 64]; 1 is the plain work-list launch.  No
+ * reference counterpart (the reference runs one work group per query tile
+ * over the whole key range, src/fused/pipeline.hpp:286-401). */
+size_t fmha_fwd_d64_splitkv_workspace_bytes(int ntiles, int num_splits);
+int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int causal,
+                                    int total_q, int total_k, const int32_t* tiles,
+                                    int ntiles, int num_splits, void* workspace,
+                                    size_t workspace_bytes, struct CUstream_st* stream);
 
 /* Allocation-free variant of fmha_fwd_d64_bf16_tiles.  No counterpart in the
  * reference.  Meant for callers that may not allocate device memory: code
