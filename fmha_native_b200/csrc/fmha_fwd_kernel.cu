@@ -42,6 +42,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -60,22 +61,40 @@ namespace {
 constexpr int kBlockM = 128;            // rows per query tile
 constexpr int kBlockN = 128;            // keys per KV tile
 constexpr int kHeadDim = 64;
-constexpr int kTilesPerCta = 2;         // query tiles per CTA
+// Query tiles per CTA.  With 1, each CTA (128 query rows, 256 threads, 256
+// TMEM columns, ~80 KB shared memory) runs two-per-SM, fully independent of
+// its neighbour; with 2, one CTA owns both tiles of an SM.
+#ifndef FMHA_TILES_PER_CTA
+#define FMHA_TILES_PER_CTA 1
+#endif
+constexpr int kTilesPerCta = FMHA_TILES_PER_CTA;
 constexpr int kRowsPerCta = kBlockM * kTilesPerCta;
-constexpr int kStages = 6;              // K/V ring slots (K_j, V_j alternate)
+constexpr int kCtasPerSm = kTilesPerCta == 1 ? 2 : 1;
+#ifndef FMHA_STAGES
+#define FMHA_STAGES (kTilesPerCta == 1 ? 4 : 6)
+#endif
+constexpr int kStages = FMHA_STAGES;    // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
-constexpr int kThreads = 384;            // 3 warpgroups
-// Register split (setmaxnreg): the CTA launches with 384 x 168 registers;
-// the two softmax groups take 208 each, the producer/MMA group 88:
-// 128 * (208 + 208 + 88) == 63488 <= 384 * 168.
-constexpr int kRegsSoftmax = 208;
-constexpr int kRegsControl = 88;
-constexpr int kWarpLoad = 8;
-constexpr int kWarpMma = 9;
-constexpr uint32_t kTmemCols = 512;
+constexpr int kSoftmaxWarps = 4 * kTilesPerCta;
+constexpr int kThreads = 128 * (kTilesPerCta + 1);  // softmax groups + control group
+// Register split (setmaxnreg): the CTA launches with kThreads x kLaunchRegs
+// registers; each softmax group takes kRegsSoftmax, the producer/MMA group
+// kRegsControl: 128 * (kTilesPerCta * kRegsSoftmax + kRegsControl) <=
+// kThreads * kLaunchRegs  (2 tiles: 128*(2*208+88) <= 384*168;
+// 1 tile: 128*(200+56) <= 256*128).
+constexpr int kRegsSoftmax = kTilesPerCta == 1 ? 200 : 208;
+constexpr int kRegsControl = kTilesPerCta == 1 ? 56 : 88;
+constexpr int kLaunchRegs = kTilesPerCta == 1 ? 128 : 168;
+static_assert(128 * (kTilesPerCta * kRegsSoftmax + kRegsControl) <= kThreads * kLaunchRegs,
+              "setmaxnreg split exceeds the launch register pool");
+constexpr int kWarpLoad = kSoftmaxWarps;
+constexpr int kWarpMma = kSoftmaxWarps + 1;
+constexpr uint32_t kTmemCols = 256 * kTilesPerCta;
 __host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i (fp32)
-__host__ __device__ constexpr uint32_t col_o(int i) { return 256u + i * 64u; }  // O_i (fp32)
-__host__ __device__ constexpr uint32_t col_p(int i) { return 384u + i * 64u; }  // P_i (bf16x2)
+__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * kTilesPerCta + i * 64u; }  // O_i
+__host__ __device__ constexpr uint32_t col_p(int i) {  // P_i (bf16x2)
+    return 192u * kTilesPerCta + i * 64u;
+}
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
@@ -109,6 +128,9 @@ struct KernelArgs {
     int stall_inject;          // test hook: producer withholds the first V tile
     unsigned long long* trace; // FMHA_TRACE builds: per-event clock64 of CTA (0,0)
     const int32_t* tiles;      // optional work list of (b*nhead_q+h, query block)
+    int m_blocks;              // query blocks per (batch, head) in a full launch
+    int head_group;            // (batch, head) pairs per L2 group of the launch order
+    int num_hb;                // batch * nhead_q
     int num_splits;            // split-KV: work item x = (tiles[x / num_splits], KV range x % num_splits)
     float* part_o;             // split-KV partial O (fp32, normalised) [item][256][64]
     float* part_lse;           // split-KV partial LSE (natural log) [item][256]
@@ -194,10 +216,18 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
         hb = a.tiles[2 * x];
         mblk = a.tiles[2 * x + 1];
     } else {
-        hb = blockIdx.x;
-        // Causal work grows with the query block index, so launch the heavy
-        // blocks first (src/fused/kernel.cpp:73,96).
-        mblk = kCausal ? (int)(gridDim.y - 1 - blockIdx.y) : (int)blockIdx.y;
+        // Launch order: (batch, head) pairs in groups of head_group whose K/V
+        // fit in L2 together; inside a group causal blocks go heaviest first
+        // across all its heads (src/fused/kernel.cpp:73,96), so the group's
+        // K/V is read from HBM about once.
+        const int mb = a.m_blocks;
+        const int lin = blockIdx.x;
+        const int g = lin / (a.head_group * mb);
+        const int r = lin - g * a.head_group * mb;
+        const int gs = min(a.head_group, a.num_hb - g * a.head_group);
+        hb = g * a.head_group + r % gs;
+        const int mrank = r / gs;
+        mblk = kCausal ? mb - 1 - mrank : mrank;
     }
     w.h = hb % a.nhead_q;
     w.b = hb / a.nhead_q;
@@ -233,7 +263,9 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
     w.j0 = 0;
     if (a.num_splits > 1) {
         // KV range of this split: an equal share of the longer tile's range.
-        const int n_all = max(w.n_kv[0], w.n_kv[1]);
+        int n_all = 0;
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) n_all = max(n_all, w.n_kv[i]);
         const int chunk = (n_all + a.num_splits - 1) / a.num_splits;
         const int jb = split * chunk;
         const int je = min(n_all, jb + chunk);
@@ -259,7 +291,7 @@ __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* t
 }
 
 template <bool kCausal, bool kVarlen>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     extern __shared__ uint8_t smem_raw[];
     SharedStorage& sm = *reinterpret_cast<SharedStorage*>(
@@ -302,11 +334,11 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     // Per-tile KV counts as scalars (a runtime-indexed array would live in
     // local memory).
     const int n_kv0 = w.n_kv[0];
-    const int n_kv1 = w.n_kv[1];
+    const int n_kv1 = kTilesPerCta > 1 ? w.n_kv[kTilesPerCta - 1] : 0;
     auto n_kv = [n_kv0, n_kv1](int i) { return i == 0 ? n_kv0 : n_kv1; };
     const int n_max = max(n_kv0, n_kv1);
 
-    if (warp >= 8) {
+    if (warp >= kSoftmaxWarps) {
     regs_dec<kRegsControl>();
     if (warp == kWarpLoad) {
         // ------------------------------------------------------ TMA producer
@@ -742,8 +774,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 template <bool kVarlen>
 __global__ void __launch_bounds__(128)
 fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
-    const int item_block = blockIdx.x / 2;          // 2 x 128 rows per block
-    const int r = (blockIdx.x & 1) * 128 + threadIdx.x;
+    constexpr int kParts = kRowsPerCta / 128;       // 128-row CTAs per query block
+    const int item_block = blockIdx.x / kParts;
+    const int r = (blockIdx.x % kParts) * 128 + threadIdx.x;
     if (item_block >= nblocks) return;
     const int hb = a.tiles[2 * item_block];
     const int mblk = a.tiles[2 * item_block + 1];
@@ -830,6 +863,18 @@ constexpr size_t kernel_smem_bytes() {
     return sizeof(SharedStorage) + 1024;
 }
 
+// Largest shared-memory carveout, so kCtasPerSm CTAs fit on one SM.
+void set_carveout() {
+    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
+                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+}
+
 int ensure_context(int dev, DeviceContext** out) {
     std::lock_guard<std::mutex> lock(g_mutex);
     if (g_encode == nullptr) {
@@ -859,6 +904,7 @@ int ensure_context(int dev, DeviceContext** out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        set_carveout();
         if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         ctx.ready = true;
     }
@@ -959,8 +1005,18 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     a.trace = g_trace;
 
     const int m_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
-    if (m_blocks > 65535) return FMHA_ERR_ARG;
-    dim3 grid((unsigned)(p->nhead_q * batch), (unsigned)m_blocks, 1);
+    const long long nblocks = (long long)m_blocks * p->nhead_q * batch;
+    if (nblocks > 0x7fffffffll) return FMHA_ERR_ARG;
+    a.m_blocks = m_blocks;
+    a.num_hb = p->nhead_q * batch;
+    {
+        // Group (batch, head) pairs so a group's K/V (read by all its blocks)
+        // fits in ~48 MB of the 126 MB L2.
+        const long long kv_bytes = (long long)(varlen ? p->seqlen_k : rows_k) * kHeadDim * 2 * 2;
+        const long long g = kv_bytes > 0 ? (48ll << 20) / kv_bytes : a.num_hb;
+        a.head_group = (int)std::max(1ll, std::min<long long>(g, a.num_hb));
+    }
+    dim3 grid((unsigned)nblocks, 1, 1);
     a.tiles = tiles;
     a.num_splits = 1;
     if (tiles != nullptr) {
@@ -984,7 +1040,7 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     }
     if (a.num_splits > 1) {
         if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
-        dim3 cgrid((unsigned)(2 * ntiles), 1, 1);
+        dim3 cgrid((unsigned)(ntiles * (kRowsPerCta / 128)), 1, 1);
         if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, 128, 0, stream>>>(a, ntiles);
         else fmha_fwd_d64_splitkv_combine<false><<<cgrid, 128, 0, stream>>>(a, ntiles);
     }
@@ -1047,6 +1103,7 @@ int noalloc_setup(int dev, int32_t** scratch) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        set_carveout();
         if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         d.scratch = static_cast<int32_t*>(ptr);
         d.ready = true;
@@ -1192,6 +1249,8 @@ int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal, 
     const bool varlen = params->seqstart_q != nullptr;
     return launch(params, batch, causal != 0, varlen, total_q, total_k, stream, tiles, ntiles);
 }
+
+int fmha_fwd_d64_rows_per_block(void) { return kRowsPerCta; }
 
 size_t fmha_fwd_d64_splitkv_workspace_bytes(int ntiles, int num_splits) {
     if (ntiles <= 0 || num_splits <= 0) return 0;

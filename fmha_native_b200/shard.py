@@ -12,15 +12,30 @@ writes disjoint rows of O / LSE.
 
 `plan_blocks` lists the blocks with costs; `partition` assigns them to ranks
 with longest-processing-time-first greedy balancing, and returns each rank's
-list heavy-first (the in-GPU order that minimises the scheduling tail).
+list head-major (blocks of one (batch, head) together, so its K/V stays in
+L2), heaviest first within a head.
 """
 from __future__ import annotations
 
 import heapq
 from typing import List, Optional, Sequence, Tuple
 
-ROWS_PER_BLOCK = 256
 ROWS_PER_TILE = 128
+
+
+def _rows_per_block() -> int:
+    """Query rows per work-list entry of the built kernel (128 or 256)."""
+    try:
+        import ctypes
+        import os
+
+        path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libfmha_b200.so")
+        return int(ctypes.CDLL(path).fmha_fwd_d64_rows_per_block())
+    except Exception:
+        return 128
+
+
+ROWS_PER_BLOCK = _rows_per_block()
 KEYS_PER_TILE = 128
 BLOCK_OVERHEAD = 2.0  # per-block prologue/epilogue, in KV-tile units
 
@@ -39,8 +54,8 @@ def _kv_tiles(r0: int, seqlen_q: int, seqlen_k: int, causal: bool) -> int:
 
 def block_cost(m: int, seqlen_q: int, seqlen_k: int, causal: bool) -> float:
     r0 = m * ROWS_PER_BLOCK
-    n = (_kv_tiles(r0, seqlen_q, seqlen_k, causal) +
-         _kv_tiles(r0 + ROWS_PER_TILE, seqlen_q, seqlen_k, causal))
+    n = sum(_kv_tiles(r0 + t * ROWS_PER_TILE, seqlen_q, seqlen_k, causal)
+            for t in range(ROWS_PER_BLOCK // ROWS_PER_TILE))
     return float(n) + BLOCK_OVERHEAD
 
 
@@ -69,7 +84,9 @@ def partition(blocks: Sequence[Block], world: int) -> List[List[Block]]:
         load, r = heapq.heappop(heap)
         parts[r].append(blk)
         heapq.heappush(heap, (load + blk[2], r))
-    return parts
+    # Launch order inside a rank: head-major (a head's blocks run together,
+    # sharing its K/V in L2), heaviest first within a head.
+    return [sorted(p, key=lambda x: (x[0], -x[2], x[1])) for p in parts]
 
 
 def loads(parts: Sequence[Sequence[Block]]) -> List[float]:

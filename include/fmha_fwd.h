@@ -116,8 +116,8 @@ int fmha_fwd_d64_bf16(const FmhaFwdParams* params, int batch, int causal,
                       int total_q, int total_k, struct CUstream_st* stream);
 
 /* Forward pass over an explicit list of query blocks: `tiles` is a device
- * array of `ntiles` int32 pairs (b*nhead_q + h, m) naming the 256-row query
- * block m of sequence b, head h.  Each listed block is computed exactly as
+ * array of `ntiles` int32 pairs (b*nhead_q + h, m) naming query block m
+ * (rows [m*R, (m+1)*R), R = fmha_fwd_d64_rows_per_block()) of sequence b, head h.  Each listed block is computed exactly as
  * by the entries above; blocks not listed are left untouched.  Used to shard
  * one problem over several GPUs (every rank holds the full K/V and runs its
  * own list, no collective) and to impose a load-balanced order.  Dense or
@@ -189,11 +189,15 @@ void fmha_fwd_d64_release(void);
 /* Human-readable text for a status code. */
 const char* fmha_fwd_d64_error_string(int status);
 
+/* Query rows per work-list entry of the built kernel (128: one 128-row query
+ * tile per CTA, two CTAs per SM).  No reference counterpart. */
+int fmha_fwd_d64_rows_per_block(void);
+
 /* Tile geometry of the B200 kernel (informational; callers need not compute
- * launch geometry).  128 query rows per tile, two tiles per CTA, 128 keys per
+ * launch geometry).  128 query rows per tile, one tile per CTA, 128 keys per
  * KV tile. */
 #define FMHA_B200_BLOCK_M 128
-#define FMHA_B200_ROWS_PER_BLOCK 256 /* query rows per work-list entry */
+#define FMHA_B200_ROWS_PER_BLOCK 128 /* query rows per work-list entry (see fmha_fwd_d64_rows_per_block) */
 #define FMHA_B200_BLOCK_N 128
 #define FMHA_B200_HEAD_DIM 64
 

@@ -36,8 +36,8 @@ def test_partition_complete_disjoint_balanced(name, world):
     L = shard.loads(parts)
     if len(blocks) >= 8 * world:
         assert max(L) <= 1.05 * sum(L) / world
-    for p in parts:  # heavy-first inside a rank
-        assert all(p[i][2] >= p[i + 1][2] for i in range(len(p) - 1))
+    for p in parts:  # head-major, heavy-first within a head
+        assert all((p[i][0], -p[i][2]) <= (p[i + 1][0], -p[i + 1][2]) for i in range(len(p) - 1))
 
 
 def test_block_costs_causal_monotone():
