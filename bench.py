@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl native|reference]
 
 One step = one forward pass over the workload.  Default workload is
-BASELINE configs[1] (B4 H16 S2048 non-causal).  Multi-GPU (torchrun, one rank
+North-star workload c2 (B4 H16 S2048 non-causal).  Multi-GPU (torchrun, one rank
 per GPU): every rank runs its own shard of a global batch that grows with N
 (weak scaling, no collective on the data path); time = max over ranks.
 

@@ -111,6 +111,13 @@ __host__ __device__ constexpr uint32_t col_p(int i) {  // P_i (bf16x2)
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
+// P is truncated to bf16 before P V, which lowers it by 0.28 % on average
+// (half a bf16 step, 2^-8 times the mean of 1/mantissa, 1/ln 4).  The
+// exponent is raised by log2(1 + 0.002818) so the truncation is centred;
+// l and the LSE see the same factor, which the LSE removes again.  Without
+// it a row dominated by one key (whose P the lazy reference leaves anywhere
+// in [1, 2^8)) loses up to 0.78 % of its output.
+constexpr float kPLog2Bias = 0.0040614f;
 // Pairs (of every 16) whose exp2 runs as a polynomial on the FMA/ALU pipes
 // instead of MUFU (unmasked tiles only).
 #ifndef FMHA_EXP_POLY_PAIRS
@@ -597,7 +604,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 m_run = m_new;
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            const float neg_ms = -m_use * scale;
+            const float neg_ms = kPLog2Bias - m_use * scale;
             // The exp loops of the two groups alternate (MUFU is shared per
             // SM sub-partition): group i starts exp(j) once the other group
             // finished its exp for the tile before (group 0: exp_1(j-1),
@@ -725,7 +732,8 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
                 const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
                 a.part_lse[prow] = (l_run > 0.0f)
-                                       ? (__log2f(l_run) + m_use * scale) * 0.69314718055994531f
+                                       ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
+                                             0.69314718055994531f
                                        : -INFINITY;
             } else if (row < w.seqlen_q) {
                 const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
@@ -757,7 +765,8 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 if (a.lse != nullptr) {
                     const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
                     const float lse = (l_run > 0.0f)
-                                          ? (__log2f(l_run) + m_use * scale) * 0.69314718055994531f
+                                          ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
+                                                0.69314718055994531f
                                           : -INFINITY;
                     long long idx;
                     if constexpr (kVarlen) {
@@ -846,7 +855,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 m_run = m_new;
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            const float neg_ms = -m_use * scale;
+            const float neg_ms = kPLog2Bias - m_use * scale;
             if (t == 0) TRACE_EV(i, j, 6);
             const float2 scale2 = make_float2(scale, scale);
             const float2 neg2 = make_float2(neg_ms, neg_ms);
@@ -928,7 +937,8 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             const float inv_l = (l_tot > 0.0f) ? 1.0f / l_tot : 0.0f;
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const float lse = (l_tot > 0.0f)
-                                  ? (__log2f(l_tot) + m_use * scale) * 0.69314718055994531f
+                                  ? (__log2f(l_tot) + m_use * scale - kPLog2Bias) *
+                                        0.69314718055994531f
                                   : -INFINITY;
             if (a.part_o != nullptr) {
                 const size_t prow = (size_t)blockIdx.x * kRowsPerCta + (size_t)i * kBlockM + t;

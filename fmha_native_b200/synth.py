@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs for the BASELINE workloads (no dataset exists for
+"""Seeded synthetic inputs for the north-star workloads (no dataset exists for
 this path; the reference benchmarks on random tensors too,
 src/bench_fmha_fwd.cpp:128-129).
 
@@ -41,7 +41,7 @@ class Workload:
 
 
 def varlen_lengths(n: int = 16, lo: int = 128, hi: int = 8192, seed: int = 7) -> list[int]:
-    """lengths uniform-integer in [lo, hi] from `seed`."""
+    """North-star varlen config: lengths uniform-integer in [lo, hi] from `seed`."""
     rng = np.random.default_rng(seed)
     return [int(x) for x in rng.integers(lo, hi + 1, size=n)]
 

@@ -13,7 +13,7 @@ baseline leg.  Nothing in the product package imports this module.
 * :func:`compare` computes the verdicts: the reference's own pass rule
   (src/runner/cpu_ref.cpp:26-28, 246-247: every |dO| <= 1e-3, max relative
   error <= 0.05 over |ref| >= 0.01, per-row cosine >= 0.99995, no non-finite)
-  and the BASELINE rule (max-abs <= 2e-2, rel-L2 <= 5e-3; LSE |d| <= 1e-3).
+  and the north-star rule (max-abs <= 2e-2, rel-L2 <= 5e-3; LSE |d| <= 1e-3).
 """
 from __future__ import annotations
 
@@ -33,7 +33,7 @@ REF_TOL_ABS = 1e-3        # cpu_ref.cpp:26
 REF_TOL_REL = 0.05        # cpu_ref.cpp:27 (|ref| >= 0.01)
 REF_TOL_COS = 0.99995     # cpu_ref.cpp:28
 LSE_TOL_ABS = 1e-3        # tests/test_fmha_fwd_d64.cpp:634
-BASE_TOL_MAX_ABS = 2e-2   # BASELINE north star
+BASE_TOL_MAX_ABS = 2e-2   # north-star tolerance
 BASE_TOL_REL_L2 = 5e-3
 
 

@@ -7,7 +7,7 @@ kept identical so a reference user recognises every case.  Inputs come from
 the reference generator (glibc srand(42), buffers.cpp:99-127) in the
 reference oracle layouts: BHSD dense, [H,total,D] varlen.
 
-BASELINE_CASES are the five configurations of the B200 north star.
+BASELINE_CASES are the five north-star configurations.
 """
 from __future__ import annotations
 

@@ -94,5 +94,5 @@ def test_known_answer_closed_form(cuda_device, sq, sk):
                                   strides_k=(D, sk * D, sk * D), strides_v=(D, sk * D, sk * D),
                                   out_shape=(1, 1, sq, D), strides_o=(D, sq * D, sq * D))
     v_ = O.compare(o_k, o_ref, lse.cpu().numpy(), lse_ref)
-    # O lies in [1, 2) here (bf16 ulp 2^-7): the BASELINE bar applies.
+    # O lies in [1, 2) here (bf16 ulp 2^-7): the north-star tolerance applies.
     assert v_["baseline_pass"] and v_["lse_pass"], v_

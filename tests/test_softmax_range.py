@@ -1,0 +1,78 @@
+"""Score distributions that stress the online softmax's reference-max
+handling: a row max that rises tile after tile, isolated key spikes whose
+jump exceeds 2^64 in P units, and a max found in the first tile only.
+
+The reference's kernel keeps an exact running max
+(src/fused/op_softmax.hpp:12, softmax_row_max at :148); this kernel moves its
+reference lazily, so these inputs check that both agree with the oracle
+(cpu_ref.cpp:86-144).  Outputs here reach |O| ~ 5, where one bf16 step
+of O is 2^-7 relative, so the element bar is 2e-2 + 2^-7 |O_ref| (the 2e-2
+north-star bar plus one relative bf16 step); rel-L2 <= 5e-3 and LSE 1e-3
+hold unchanged.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import fmha_native_b200 as fm
+import oracle as O
+from harness import D, from_device_bf16, to_device_bf16
+
+pytestmark = pytest.mark.gpu
+
+S = 1024
+H = 2
+
+
+def _inputs(kind: str, seed: int):
+    rng = np.random.default_rng(seed)
+    common = np.ones(D, np.float32)
+    q = rng.standard_normal((H, S, D)).astype(np.float32)
+    k = rng.standard_normal((H, S, D)).astype(np.float32)
+    v = rng.standard_normal((H, S, D)).astype(np.float32)
+    if kind == "rising":
+        # Key norms grow 1x -> 4x across the sequence: the row max climbs a
+        # few log2 units per 128-key tile.
+        k *= (1.0 + 3.0 * np.arange(S, dtype=np.float32) / S)[None, :, None]
+        q *= 2.0
+    elif kind == "spikes":
+        # Every query shares a common component; keys aligned with it give
+        # jumps of roughly 35, 58 and 92 log2 units, then one of ~140.
+        q += common
+        for pos, mag in ((200, 3.0), (450, 5.0), (700, 8.0), (950, 12.0)):
+            k[:, pos] = mag * common
+    elif kind == "falling":
+        q += common
+        k[:, 5] = 8.0 * common
+    else:
+        raise ValueError(kind)
+    bits = [O.f32_to_bf16_bits_trunc(x.ravel()) for x in (q, k, v)]
+    return bits
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("kind", ["rising", "spikes", "falling"])
+def test_reference_max_moves(cuda_device, kind, causal):
+    import torch
+
+    q, k, v = _inputs(kind, 1234)
+    shape = (1, H, S, D)
+    qd, kd, vd = (to_device_bf16(x, shape, cuda_device) for x in (q, k, v))
+    od = torch.full(shape, float("nan"), device=cuda_device, dtype=torch.bfloat16)
+    lse = torch.full((1, H, S), float("nan"), device=cuda_device, dtype=torch.float32)
+    params, batch, _, _ = fm.params_from_tensors(qd, kd, vd, od, lse, "bhsd")
+    assert fm.call_entry(params, batch, causal, False) == fm.FMHA_OK
+    torch.cuda.synchronize()
+    assert fm.status(0) == fm.FMHA_OK
+    o_k = O.bf16_bits_to_f32(from_device_bf16(od)).reshape(shape)
+    st = (D, S * D, H * S * D)
+    o_ref, lse_ref = O.oracle_fwd(q, k, v, batch=1, nhead_q=H, nhead_k=H, seqlen_q=S,
+                                  seqlen_k=S, causal=causal, strides_q=st, strides_k=st,
+                                  strides_v=st, out_shape=shape, strides_o=st)
+    verdict = O.compare(o_k, o_ref, lse.cpu().numpy(), lse_ref)
+    over = np.abs(o_k - o_ref) - (2e-2 + 2.0 ** -7 * np.abs(o_ref))
+    verdict["worst_over_bar"] = float(over.max())
+    assert verdict["nonfinite"] == 0, verdict
+    assert (over <= 0).all(), verdict
+    assert verdict["rel_l2"] <= 5e-3 and verdict["lse_pass"], verdict
