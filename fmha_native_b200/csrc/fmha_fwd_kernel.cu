@@ -1,31 +1,33 @@
 // fmha_fwd_kernel.cu -- B200 (sm_100a) head-dim-64 BF16 fused attention
 // forward, and the C-ABI launchers declared in include/fmha_fwd.h.
 //
-// One CTA owns two 128-row query tiles of one (batch, head) and walks the
-// key/value sequence in 128-key tiles.  It is warp specialised:
+// One CTA owns one 128-row query tile of one (batch, head) and walks the
+// key/value sequence in 128-key tiles; two CTAs share each SM, each with its
+// own pipeline.  The CTA is warp specialised:
 //
-//   warps 0-3  softmax group 0  : rows of query tile 0 (one row per thread)
-//   warps 4-7  softmax group 1  : rows of query tile 1
-//   warp  8    TMA producer     : Q tiles once, then K_j / V_j into a ring
-//   warp  9    MMA issuer       : one thread issues every tcgen05.mma; the
-//                                 warp also owns the TMEM allocation
+//   warps 0-3  softmax          : one query row per thread (TMEM lane = row)
+//   warp  4    TMA producer     : Q once, then K_j / V_j into a 4-slot ring
+//   warp  5    MMA issuer       : one elected lane issues every tcgen05.mma;
+//                                 the warp also owns the TMEM allocation
+//   warps 6-7  idle             : complete the control warpgroup for setmaxnreg
 //
-// Tensor memory (512 columns x 128 lanes, fp32):
-//   [  0,128) S0 = Q0 K^T   (its first 64 columns are reused for P0 as bf16x2)
-//   [128,256) S1 = Q1 K^T   (P1 likewise)
-//   [256,320) O0 accumulator
-//   [320,384) O1 accumulator
+// Tensor memory (256 columns x 128 lanes per CTA; two CTAs fill the SM):
+//   [  0,128) S = Q K^T (fp32)
+//   [128,192) O accumulator (fp32)
+//   [192,256) P (bf16x2)
 //
-// Per KV tile j and query tile i the schedule is
-//   MMA : S_i = Q_i K_j^T  -> commit(s_full[i])
-//   SM_i: S -> row max -> (lazy) rescale O_i -> P = exp2(S*scale - m*scale)
-//         -> bf16 P into TMEM -> arrive(p_full[i])
-//   MMA : O_i += P_i V_j, then S_i = Q_i K_{j+1}^T immediately
-// so the two softmax groups run half a period apart and the tensor core
-// alternates between them.  tcgen05 MMAs issued by one thread execute in
-// order, so S_i(j+1) overwriting P_i(j) is safe once O_i += P_i V_j is issued,
-// and s_full[i] (committed after S_i(j+1)) also proves O_i += P_i V_j is
-// complete, which is what makes the softmax-side O rescale race free.
+// Per KV tile j the schedule is
+//   MMA : S = Q K_j^T -> commit(s_full)
+//   SM  : S -> registers -> arrive(s_free) -> mask, row max, (lazy) rescale
+//         of O -> P = exp2(S*scale - m*scale) -> wait(pv_done of j-1) ->
+//         bf16 P into TMEM -> arrive(p_full)
+//   MMA : S = Q K_{j+1}^T as soon as s_free arrives, then O += P V_j ->
+//         commit(pv_done)
+// tcgen05 MMAs issued by one thread execute in order, so pv_done(j-1) also
+// proves every earlier MMA finished, which is what makes the softmax-side O
+// rescale race free.  (Build flag FMHA_TILES_PER_CTA=2 keeps the older
+// layout: one CTA per SM with two query tiles sharing one producer and MMA
+// warp.)
 //
 // Reference semantics followed (poyenc/fmha_native):
 //   grid decode + causal heavy-first order ... src/fused/kernel.cpp:55-99
@@ -75,13 +77,7 @@ constexpr int kCtasPerSm = kTilesPerCta == 1 ? 2 : 1;
 #endif
 constexpr int kStages = FMHA_STAGES;    // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
-// FMHA_SPLIT_ROWS: eight softmax warps per query tile, two threads per row
-// (each owns 64 of the 128 key columns of a tile), instead of four warps with
-// one thread per row.
-#ifndef FMHA_SPLIT_ROWS
-#define FMHA_SPLIT_ROWS 0
-#endif
-constexpr int kWarpsPerTile = FMHA_SPLIT_ROWS ? 8 : 4;
+constexpr int kWarpsPerTile = 4;   // softmax warps per query tile: one thread per row
 constexpr int kSoftmaxWarps = kWarpsPerTile * kTilesPerCta;
 constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax groups + control group
 // Register split (setmaxnreg): the CTA launches with kThreads x kLaunchRegs
@@ -90,14 +86,14 @@ constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax groups + control 
 // kThreads * kLaunchRegs  (2 tiles: 128*(2*208+88) <= 384*168;
 // 1 tile: 128*(192+64) <= 256*128; 200/56 spilled in the control warps).
 #ifndef FMHA_REGS_SOFTMAX
-#define FMHA_REGS_SOFTMAX (FMHA_SPLIT_ROWS ? 104 : (kTilesPerCta == 1 ? 192 : 208))
+#define FMHA_REGS_SOFTMAX (kTilesPerCta == 1 ? 192 : 208)
 #endif
 #ifndef FMHA_REGS_CONTROL
-#define FMHA_REGS_CONTROL (FMHA_SPLIT_ROWS ? 32 : (kTilesPerCta == 1 ? 64 : 88))
+#define FMHA_REGS_CONTROL (kTilesPerCta == 1 ? 64 : 88)
 #endif
 constexpr int kRegsSoftmax = FMHA_REGS_SOFTMAX;
 constexpr int kRegsControl = FMHA_REGS_CONTROL;
-constexpr int kLaunchRegs = FMHA_SPLIT_ROWS ? 80 : (kTilesPerCta == 1 ? 128 : 168);
+constexpr int kLaunchRegs = kTilesPerCta == 1 ? 128 : 168;
 static_assert(32 * kSoftmaxWarps * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs,
               "setmaxnreg split exceeds the launch register pool");
 constexpr int kWarpLoad = kSoftmaxWarps;
@@ -178,8 +174,6 @@ struct alignas(1024) SharedStorage {
     uint64_t bar_sfree[kTilesPerCta];  // S_i read into registers (128 arrivals)
     uint64_t bar_p[kTilesPerCta];      // P_i written, O_i rescaled (128 arrivals)
     uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
-    uint64_t bar_turn[kTilesPerCta];   // exp-phase hand-off between the two
-                                       // softmax groups (one arrival per warp)
     uint64_t bar_o[kTilesPerCta];
     uint64_t bar_drain;
     uint32_t tmem_base;
@@ -331,7 +325,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             mbar_init(smem_u32(&sm.bar_sfree[i]), 32 * kWarpsPerTile);
             mbar_init(smem_u32(&sm.bar_p[i]), 32 * kWarpsPerTile);
             mbar_init(smem_u32(&sm.bar_pv[i]), 1);
-            mbar_init(smem_u32(&sm.bar_turn[i]), 4);
             mbar_init(smem_u32(&sm.bar_o[i]), 1);
         }
         for (int s = 0; s < kStages; ++s) {
@@ -530,7 +523,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         __syncwarp();
     }
     } else {
-#if !FMHA_SPLIT_ROWS
         regs_inc<kRegsSoftmax>();
         // ------------------------------------------------------ softmax groups
         const int i = warp >> 2;                    // query tile of this group
@@ -605,25 +597,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const float neg_ms = kPLog2Bias - m_use * scale;
-            // The exp loops of the two groups alternate (MUFU is shared per
-            // SM sub-partition): group i starts exp(j) once the other group
-            // finished its exp for the tile before (group 0: exp_1(j-1),
-            // group 1: exp_0(j)), and signals when done.
-#ifndef FMHA_EXP_ALTERNATE
-#define FMHA_EXP_ALTERNATE 0
-#endif
-            if (FMHA_EXP_ALTERNATE) {
-                const int other_n = n_kv(i ^ 1);
-                const int need = i == 0 ? j - 1 : j;  // other group's tile to wait for
-                if (need >= 0 && need < other_n) {
-                    got = wait_phase(smem_u32(&sm.bar_turn[i]), need & 1, abort_flag, a,
-                                     kErrTimeoutSoftmax);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        ok = false;
-                        break;
-                    }
-                }
-            }
             if (t == 0) TRACE_EV(i, j, 6);
             const float2 scale2 = make_float2(scale, scale);
             const float2 neg2 = make_float2(neg_ms, neg_ms);
@@ -656,8 +629,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             };
             if (need_mask) exp_tile(std::false_type{});
             else exp_tile(std::true_type{});
-            __syncwarp();
-            if (FMHA_EXP_ALTERNATE && lane == 0) mbar_arrive(smem_u32(&sm.bar_turn[i ^ 1]));
             const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
             l_run = fmaf(l_run, alpha, s01.x + s01.y);
             if (t == 0) TRACE_EV(i, j, 3);
@@ -778,218 +749,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
             }
         }
-    #else
-        regs_inc<kRegsSoftmax>();
-        // ------------------------------------------------------ softmax groups
-        // Eight warps per query tile.  Warp w covers TMEM lanes (rows)
-        // 32*(w%4) + 16*((w/4)%2) + [0,16); with the 16x32bx2 access shape
-        // threads t and t+16 of the warp share a row and hold its key columns
-        // [0,64) and [64,128), so row reductions are one shuffle.
-        const int i = warp >> 3;                     // query tile
-        const int quarter = warp & 3;                // TMEM lane quarter of this warp
-        const int half = (warp >> 2) & 1;            // 16-lane half of the quarter
-        const int cpart = lane >> 4;                 // which half of the row's columns
-        const int t = quarter * 32 + half * 16 + (lane & 15);  // row inside the tile
-        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32 + half * 16) << 16;
-        const uint32_t tS = tmem + lane_base + col_s(i);
-        const uint32_t tO = tmem + lane_base + col_o(i);
-        const uint32_t tP = tmem + lane_base + col_p(i);
-        const int n = n_kv(i);
-        const int tile_row0 = w.row0 + i * kBlockM;
-        const int row = tile_row0 + t;
-        const int shift = w.seqlen_k - w.seqlen_q;
-        const float scale = a.scale;
-        const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
-
-        float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
-        float l_run = 0.0f;       // this thread's share of the running sum of P
-        bool ok = true;
-
-        for (int j = 0; j < n; ++j) {
-            if (t == 0) TRACE_EV(i, j, 0);
-            bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
-            if (t == 0) TRACE_EV(i, j, 1);
-            if (!__all_sync(0xffffffffu, got)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t r[2][32];  // columns cpart*64 + [0,32) and + [32,64)
-            tmem_ld_16x32bx2<64>(tS, r[0]);
-            tmem_ld_16x32bx2<64>(tS + 32, r[1]);
-            tmem_wait_ld();
-            reg_fence(r[0]);
-            reg_fence(r[1]);
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sm.bar_sfree[i]));
-            if (t == 0) TRACE_EV(i, j, 2);
-
-            const int k0 = (w.j0 + j) * kBlockN + cpart * 64;
-            const int kt0 = (w.j0 + j) * kBlockN;
-            const bool need_mask = (kt0 + kBlockN > w.seqlen_k) ||
-                                   (kCausal && kt0 + kBlockN - 1 > tile_row0 + shift);
-            if (need_mask) {
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
-            }
-            float mx[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
-                mx[q] = __uint_as_float(rr[0]);
-#pragma unroll
-                for (int e = 1; e < 15; e += 2)
-                    mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
-                mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
-            }
-            float row_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-            row_max = fmaxf(row_max, __shfl_xor_sync(0xffffffffu, row_max, 16));
-            const float m_new = fmaxf(m_run, row_max);
-            const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
-            float alpha = 1.0f;
-            if (upd) {
-                alpha = ex2_approx((m_run - m_new) * scale);
-                m_run = m_new;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            const float neg_ms = kPLog2Bias - m_use * scale;
-            if (t == 0) TRACE_EV(i, j, 6);
-            const float2 scale2 = make_float2(scale, scale);
-            const float2 neg2 = make_float2(neg_ms, neg_ms);
-            float2 sum[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
-            uint32_t p[32];  // packed bf16 P of this thread's 64 columns
-            auto exp_tile = [&](auto poly_tag) {
-                constexpr bool kPoly = decltype(poly_tag)::value;
-#pragma unroll
-                for (int c = 0; c < 2; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const int pr = e >> 1;
-                        const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
-                                                           __uint_as_float(r[c][e + 1])),
-                                               scale2, neg2);
-                        float2 pp;
-                        if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
-                            pp = exp2_poly2(x);
-                        else
-                            pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                        sum[pr & 3] = fadd2(sum[pr & 3], pp);
-                        p[c * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
-                    }
-            };
-            if (need_mask) exp_tile(std::false_type{});
-            else exp_tile(std::true_type{});
-            const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
-            l_run = fmaf(l_run, alpha, s01.x + s01.y);
-            if (t == 0) TRACE_EV(i, j, 3);
-
-            if (j > 0) {
-                got = wait_phase(smem_u32(&sm.bar_pv[i]), (j - 1) & 1, abort_flag, a,
-                                 kErrTimeoutSoftmax);
-                if (!__all_sync(0xffffffffu, got)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-            }
-            if (t == 0) TRACE_EV(i, j, 4);
-            tmem_st_16x32bx2<32>(tP, p);
-            if (j > 0 && __any_sync(0xffffffffu, upd)) {
-                // This thread rescales O columns cpart*32 + [0,32) of its row.
-                uint32_t o[32];
-                tmem_ld_16x32bx2<32>(tO, o);
-                tmem_wait_ld();
-                reg_fence(o);
-                const float2 a2 = make_float2(alpha, alpha);
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    const float2 v2 = fmul2(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
-                    o[e] = __float_as_uint(v2.x);
-                    o[e + 1] = __float_as_uint(v2.y);
-                }
-                tmem_st_16x32bx2<32>(tO, o);
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sm.bar_p[i]));
-            if (t == 0) TRACE_EV(i, j, 5);
-        }
-
-        // ---------------------------------------------------- epilogue
-        if (ok && n > 0) {
-            bool got = wait_phase(smem_u32(&sm.bar_o[i]), 0, abort_flag, a, kErrTimeoutSoftmax);
-            ok = __all_sync(0xffffffffu, got);
-        }
-        if (ok) {
-            uint32_t o[32];  // O columns cpart*32 + [0,32)
-            if (n > 0) {
-                tc_fence_after();
-                tmem_ld_16x32bx2<32>(tO, o);
-                tmem_wait_ld();
-                reg_fence(o);
-            }
-            const float l_tot = l_run + __shfl_xor_sync(0xffffffffu, l_run, 16);
-            const float inv_l = (l_tot > 0.0f) ? 1.0f / l_tot : 0.0f;
-            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            const float lse = (l_tot > 0.0f)
-                                  ? (__log2f(l_tot) + m_use * scale - kPLog2Bias) *
-                                        0.69314718055994531f
-                                  : -INFINITY;
-            if (a.part_o != nullptr) {
-                const size_t prow = (size_t)blockIdx.x * kRowsPerCta + (size_t)i * kBlockM + t;
-                float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim + cpart * 32);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    float v[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        v[e] = n > 0 ? __uint_as_float(o[c * 4 + e]) * inv_l : 0.0f;
-                    dst[c] = make_float4(v[0], v[1], v[2], v[3]);
-                }
-                if (cpart == 0) a.part_lse[prow] = lse;
-            } else if (row < w.seqlen_q) {
-                uint16_t* orow;
-                if constexpr (kVarlen) {
-                    orow = a.o + (long long)w.h * a.nhead_stride_o +
-                           (long long)(w.off_q + row) * a.stride_o;
-                } else {
-                    orow = a.o + (long long)w.b * a.batch_stride_o +
-                           (long long)w.h * a.nhead_stride_o + (long long)row * a.stride_o;
-                }
-                uint4* dst = reinterpret_cast<uint4*>(orow + cpart * 32);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int col = c * 8 + e * 2;
-                        const float v0 = n > 0 ? __uint_as_float(o[col]) * inv_l : 0.0f;
-                        const float v1 = n > 0 ? __uint_as_float(o[col + 1]) * inv_l : 0.0f;
-#ifdef FMHA_O_ROUND_TRUNC
-                        pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
-#else
-                        pk[e] = pack_bf16_rne(v0, v1);
-#endif
-                    }
-                    dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                }
-                if (a.lse != nullptr && cpart == 0) {
-                    long long idx;
-                    if constexpr (kVarlen) {
-                        idx = (long long)w.h * a.total_q + w.off_q + row;
-                    } else {
-                        idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
-                    }
-                    a.lse[idx] = lse;
-                }
-            }
-        }
-#endif
 }
 
     // ---------------------------------------------------------- teardown
