@@ -217,12 +217,21 @@ def native_arm(args, workload_key):
         share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
     splits = 1
     workspace = None
+    items = None
     if tiles is not None:
-        # split-KV when this rank's blocks cannot fill the GPU (long causal, few heads)
-        splits = args.splits if args.splits > 0 else shd.choose_splits(tiles.shape[0])
-        if splits > 1:
-            workspace = torch.empty(fm.splitkv_workspace_bytes(tiles.shape[0], splits) // 4,
-                                    device=dev, dtype=torch.float32)
+        if args.splits > 0:
+            # uniform split-KV (every block cut into `splits` equal KV ranges)
+            splits = args.splits
+            if splits > 1:
+                workspace = torch.empty(fm.splitkv_workspace_bytes(tiles.shape[0], splits) // 4,
+                                        device=dev, dtype=torch.float32)
+        else:
+            # per-block split-KV: blocks longer than ~2 items per CTA slot are cut
+            plan = shd.plan_items(part)
+            if any(it[3] >= 0 for it in plan):
+                items = torch.from_numpy(shd.items_array(plan)).to(dev)
+                workspace = torch.empty(fm.items_workspace_bytes(items.shape[0]) // 4,
+                                        device=dev, dtype=torch.float32)
     layout = w.layout
     o = torch.empty_like(q)
     lse = None
@@ -237,7 +246,10 @@ def native_arm(args, workload_key):
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
 
     def step():
-        if tiles is not None and splits > 1:
+        if items is not None:
+            st = fm.call_items(params, batch, w.causal, items.data_ptr(), items.shape[0],
+                               workspace.data_ptr(), workspace.numel() * 4, tq, tk, sh)
+        elif tiles is not None and splits > 1:
             st = fm.call_tiles_splitkv(params, batch, w.causal, tiles.data_ptr(), tiles.shape[0],
                                        splits, workspace.data_ptr(), workspace.numel() * 4, tq, tk, sh)
         elif tiles is not None:
@@ -288,7 +300,7 @@ def native_arm(args, workload_key):
     achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API, copies inside the timed region
-    e2e = e2e_measure(fm, w, dev, args, tiles, splits)
+    e2e = e2e_measure(fm, w, dev, args, tiles, splits, items)
     if world > 1:
         t = torch.tensor([e2e["ms"]], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -310,7 +322,10 @@ def native_arm(args, workload_key):
             "config": {"workload": w.name, "per_gpu_batch": w.batch if not args.shard else None,
                        "global_batch": w.batch if args.shard else w.batch * world,
                        "heads": w.heads, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
-                       "lse": w.lse, "splitkv": splits, "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
+                       "lse": w.lse,
+                       "splitkv": (f"per-block: {items.shape[0]} items, "
+                                   f"{int((items[:, 3] >= 0).sum().item())} partial"
+                                   if items is not None else splits), "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
                                        "no collective" if args.shard else
                                        f"{world} independent replicas (weak scaling), no collective"), "l2": "flushed (256 MiB write) between steps"},
             "pct_of_bf16_peak": round(100.0 * (value / world) / peak_tf, 2),
@@ -332,7 +347,7 @@ def native_arm(args, workload_key):
     return 0
 
 
-def e2e_measure(fm, w, dev, args, tiles=None, splits=1):
+def e2e_measure(fm, w, dev, args, tiles=None, splits=1, items=None):
     """Public API with pinned host buffers: H2D of Q,K,V (and cu_seqlens),
     the kernel, D2H of O (and LSE) -- all inside CUDA events."""
     import torch
@@ -358,7 +373,8 @@ def e2e_measure(fm, w, dev, args, tiles=None, splits=1):
             dcu.copy_(hcu, non_blocking=True)
         o = fm.fmha_fwd(dq, dk, dv, causal=w.causal, return_lse=False, layout=w.layout,
                         cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream,
-                        out=do, tiles=tiles, num_splits=splits)
+                        out=do, tiles=None if items is not None else tiles,
+                        num_splits=splits, items=items)
         ho.copy_(o, non_blocking=True)
 
     for _ in range(2):

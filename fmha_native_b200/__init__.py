@@ -30,7 +30,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libfmha_b200.so")
 
 LOG2E = 1.4426950408889634
 HEAD_DIM = 64
-BLOCK_M = 128          # query rows per tile (two tiles per CTA)
+BLOCK_M = 128          # query rows per tile (one tile per CTA)
 BLOCK_N = 128          # keys per KV tile
 
 FMHA_OK = 0
@@ -49,6 +49,8 @@ ENTRY_POINTS = (
     "fmha_fwd_d64_bf16_tiles",
     "fmha_fwd_d64_bf16_tiles_splitkv",
     "fmha_fwd_d64_splitkv_workspace_bytes",
+    "fmha_fwd_d64_bf16_items",
+    "fmha_fwd_d64_items_workspace_bytes",
     "fmha_fwd_d64_status",
     "fmha_fwd_d64_set_wait_limit_ns",
     "fmha_fwd_d64_release",
@@ -116,6 +118,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fmha_fwd_d64_bf16_tiles_splitkv.restype = ctypes.c_int
     lib.fmha_fwd_d64_splitkv_workspace_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
     lib.fmha_fwd_d64_splitkv_workspace_bytes.restype = ctypes.c_size_t
+    lib.fmha_fwd_d64_bf16_items.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.fmha_fwd_d64_bf16_items.restype = ctypes.c_int
+    lib.fmha_fwd_d64_items_workspace_bytes.argtypes = [ctypes.c_int]
+    lib.fmha_fwd_d64_items_workspace_bytes.restype = ctypes.c_size_t
     lib.fmha_fwd_d64_status.argtypes = [ctypes.c_void_p]
     lib.fmha_fwd_d64_status.restype = ctypes.c_int
     lib.fmha_fwd_d64_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
@@ -219,6 +227,21 @@ def call_tiles_splitkv(params: FmhaFwdParams, batch: int, causal: bool, tiles_pt
         ctypes.c_void_p(stream))
 
 
+def items_workspace_bytes(n_items: int) -> int:
+    return int(load_library().fmha_fwd_d64_items_workspace_bytes(n_items))
+
+
+def call_items(params: FmhaFwdParams, batch: int, causal: bool, items_ptr: int, n_items: int,
+               workspace_ptr: int, workspace_bytes: int, total_q: int = 0, total_k: int = 0,
+               stream: int = 0) -> int:
+    """Call fmha_fwd_d64_bf16_items on a device int32 [n_items, 4] item list
+    (b*nhead_q + h, query block, kv_begin, kv_end); see shard.plan_items."""
+    lib = load_library()
+    return lib.fmha_fwd_d64_bf16_items(
+        ctypes.byref(params), batch, int(causal), total_q, total_k, ctypes.c_void_p(items_ptr),
+        n_items, ctypes.c_void_p(workspace_ptr), workspace_bytes, ctypes.c_void_p(stream))
+
+
 def status(stream: int = 0) -> int:
     """Synchronise `stream` and read/clear the device error word."""
     return load_library().fmha_fwd_d64_status(ctypes.c_void_p(stream))
@@ -271,7 +294,7 @@ def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
 
 def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: str = "bshd",
              cu_seqlens_q=None, cu_seqlens_k=None, out=None, lse_out=None, stream=None,
-             tiles=None, num_splits: int = 1, workspace=None):
+             tiles=None, num_splits: int = 1, workspace=None, items=None):
     """O = softmax(Q K^T / 8) V on the B200 kernel (head_dim 64, bf16).
 
     Dense: q [B,Sq,Hq,64] ("bshd") or [B,Hq,Sq,64] ("bhsd"); varlen: q
@@ -282,6 +305,9 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
     `num_splits` > 1 (with `tiles`) splits each block's key range (split-KV);
     `workspace` is then a device buffer of splitkv_workspace_bytes() bytes
     (allocated here when omitted).
+    `items`: optional device int32 [n, 4] work-item list with per-item KV
+    ranges (fmha_native_b200.shard.plan_items); `workspace` then holds
+    items_workspace_bytes(n) bytes (allocated here when omitted).
     """
     import torch
 
@@ -304,7 +330,14 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
                               dtype=torch.float32)
     params, batch, tq, tk = params_from_tensors(q, k, v, o, lse, layout, cu_seqlens_q, cu_seqlens_k)
     s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
-    if tiles is not None and num_splits > 1:
+    if items is not None:
+        nbytes = items_workspace_bytes(items.shape[0])
+        if workspace is None:
+            workspace = torch.empty(max(nbytes, 16) // 4, device=q.device, dtype=torch.float32)
+        _check(call_items(params, batch, causal, items.data_ptr(), items.shape[0],
+                          workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                          tq, tk, s), "fmha_fwd(items)")
+    elif tiles is not None and num_splits > 1:
         nbytes = splitkv_workspace_bytes(tiles.shape[0], num_splits)
         if workspace is None:
             workspace = torch.empty(nbytes // 4, device=q.device, dtype=torch.float32)

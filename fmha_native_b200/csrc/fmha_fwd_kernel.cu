@@ -148,8 +148,9 @@ struct KernelArgs {
     int head_group;            // (batch, head) pairs per L2 group of the launch order
     int num_hb;                // batch * nhead_q
     int num_splits;            // split-KV: work item x = (tiles[x / num_splits], KV range x % num_splits)
-    float* part_o;             // split-KV partial O (fp32, normalised) [item][256][64]
-    float* part_lse;           // split-KV partial LSE (natural log) [item][256]
+    const int32_t* items;      // optional work items (b*nhead_q+h, query block, kv_begin, kv_end)
+    float* part_o;             // split-KV partial O (fp32, normalised) [item][128][64]
+    float* part_lse;           // split-KV partial LSE (natural log) [item][128]
 };
 
 // Pipeline event timestamps (diagnostic builds only, -DFMHA_TRACE): slot
@@ -216,13 +217,21 @@ struct TileWork {
     int seqlen_q, seqlen_k;
     int off_q, off_k;           // varlen packed-row offsets
     int b, h, kvh;
+    bool partial;               // split-KV item: partial O/LSE into the workspace
 };
 
 template <bool kCausal, bool kVarlen>
 __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
     int hb, mblk;
     int split = 0;
-    if (a.tiles != nullptr) {
+    int kv_begin = 0, kv_end = -1;  // work items: explicit KV-tile range (end < 0: all)
+    if (a.items != nullptr) {
+        const int4 it = reinterpret_cast<const int4*>(a.items)[blockIdx.x];
+        hb = it.x;
+        mblk = it.y;
+        kv_begin = it.z;
+        kv_end = it.w;
+    } else if (a.tiles != nullptr) {
         // Caller-supplied work list: (batch*nhead_q + head, query block); in
         // split-KV mode every entry expands into num_splits KV ranges.
         const int x = a.num_splits > 1 ? (int)blockIdx.x / a.num_splits : (int)blockIdx.x;
@@ -275,7 +284,13 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
         w.n_kv[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
     }
     w.j0 = 0;
-    if (a.num_splits > 1) {
+    w.partial = a.num_splits > 1 || (a.items != nullptr && kv_end >= 0);
+    if (a.items != nullptr && kv_end >= 0) {
+        const int jb = max(0, kv_begin);
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], kv_end) - jb);
+        w.j0 = jb;
+    } else if (a.num_splits > 1) {
         // KV range of this split: an equal share of the longer tile's range.
         int n_all = 0;
 #pragma unroll
@@ -685,7 +700,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 reg_fence(o[0]);
                 reg_fence(o[1]);
             }
-            if (a.part_o != nullptr) {
+            if (w.partial) {
                 // Split-KV: this item's normalised partial O (fp32) and LSE;
                 // the combine kernel merges the splits of each query block.
                 const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
@@ -761,19 +776,14 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 }
 
 
-// Split-KV combine: one thread per query row of every listed block.
-// LSE = log(sum_s exp(lse_s)); O = sum_s exp(lse_s - LSE) * O_s, rounded to
-// bf16 like the main epilogue; the same LSE merge the reference's base-2
-// epilogue formula implies (src/fused/op_epilog.hpp:92-98).
+// Split-KV merge of one query row: partial slots [slot0, slot0 + nparts) of
+// query block mblk of (batch, head) hb; LSE = log(sum_s exp(lse_s)),
+// O = sum_s exp(lse_s - LSE) * O_s, rounded to bf16 like the main epilogue;
+// the same LSE merge the reference's base-2 epilogue formula implies
+// (src/fused/op_epilog.hpp:92-98).
 template <bool kVarlen>
-__global__ void __launch_bounds__(128)
-fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
-    constexpr int kParts = kRowsPerCta / 128;       // 128-row CTAs per query block
-    const int item_block = blockIdx.x / kParts;
-    const int r = (blockIdx.x % kParts) * 128 + threadIdx.x;
-    if (item_block >= nblocks) return;
-    const int hb = a.tiles[2 * item_block];
-    const int mblk = a.tiles[2 * item_block + 1];
+__device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk, int slot0,
+                                          int nparts, int r) {
     const int h = hb % a.nhead_q, b = hb / a.nhead_q;
     int seqlen_q = a.seqlen_q, off_q = 0;
     if constexpr (kVarlen) {
@@ -782,17 +792,16 @@ fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) 
     }
     const int row = mblk * kRowsPerCta + r;
     if (row >= seqlen_q) return;
-    const int S = a.num_splits;
     float mx = -INFINITY;
-    for (int s = 0; s < S; ++s)
-        mx = fmaxf(mx, a.part_lse[(size_t)(item_block * S + s) * kRowsPerCta + r]);
+    for (int s = 0; s < nparts; ++s)
+        mx = fmaxf(mx, a.part_lse[(size_t)(slot0 + s) * kRowsPerCta + r]);
     float acc[kHeadDim];
 #pragma unroll
     for (int d = 0; d < kHeadDim; ++d) acc[d] = 0.0f;
     float wsum = 0.0f;
     if (mx != -INFINITY) {
-        for (int s = 0; s < S; ++s) {
-            const size_t prow = (size_t)(item_block * S + s) * kRowsPerCta + r;
+        for (int s = 0; s < nparts; ++s) {
+            const size_t prow = (size_t)(slot0 + s) * kRowsPerCta + r;
             const float l = a.part_lse[prow];
             if (l == -INFINITY) continue;
             const float wgt = __expf(l - mx);
@@ -836,6 +845,40 @@ fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) 
                                       : ((long long)b * a.nhead_q + h) * a.seqlen_q + row;
         a.lse[idx] = lse;
     }
+}
+
+// Uniform split-KV combine: block g merges slots [g*S, g*S + S) of tiles[g].
+template <bool kVarlen>
+__global__ void __launch_bounds__(128)
+fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
+    constexpr int kParts = kRowsPerCta / 128;       // 128-row CTAs per query block
+    const int item_block = blockIdx.x / kParts;
+    const int r = (blockIdx.x % kParts) * 128 + threadIdx.x;
+    if (item_block >= nblocks) return;
+    merge_row<kVarlen>(a, a.tiles[2 * item_block], a.tiles[2 * item_block + 1],
+                       item_block * a.num_splits, a.num_splits, r);
+}
+
+// Work-item combine: block x merges the run of consecutive partial items of
+// one query block that starts at item x (other blocks return at once).
+template <bool kVarlen>
+__global__ void __launch_bounds__(128)
+fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
+    const int x = blockIdx.x;
+    const int4* items = reinterpret_cast<const int4*>(a.items);
+    const int4 it = items[x];
+    if (it.w < 0) return;  // direct item: O already written
+    if (x > 0) {
+        const int4 prev = items[x - 1];
+        if (prev.w >= 0 && prev.x == it.x && prev.y == it.y) return;  // not the run's head
+    }
+    int n = 1;
+    while (x + n < n_items) {
+        const int4 nx = items[x + n];
+        if (nx.w < 0 || nx.x != it.x || nx.y != it.y) break;
+        ++n;
+    }
+    merge_row<kVarlen>(a, it.x, it.y, x, n, threadIdx.x);
 }
 
 // ====================================================================== host
@@ -935,7 +978,8 @@ bool stride_ok(long long s, int extent) {
 
 int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
            cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1,
-           int num_splits = 1, float* workspace = nullptr) {
+           int num_splits = 1, float* workspace = nullptr, const int32_t* items = nullptr,
+           int n_items = 0) {
     if (p == nullptr || batch <= 0) return FMHA_ERR_ARG;
     if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
     if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
@@ -1023,6 +1067,13 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
             grid = dim3((unsigned)(ntiles * num_splits), 1, 1);
         }
     }
+    if (items != nullptr) {
+        if (n_items == 0) return FMHA_OK;
+        a.items = items;
+        a.part_o = workspace;
+        a.part_lse = workspace + (size_t)n_items * kRowsPerCta * kHeadDim;
+        grid = dim3((unsigned)n_items, 1, 1);
+    }
     dim3 block(kThreads);
     const size_t smem = kernel_smem_bytes<false, false>();
     if (causal) {
@@ -1032,7 +1083,12 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
         if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
         else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
     }
-    if (a.num_splits > 1) {
+    if (items != nullptr) {
+        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
+        dim3 cgrid((unsigned)n_items, 1, 1);
+        if (varlen) fmha_fwd_d64_items_combine<true><<<cgrid, 128, 0, stream>>>(a, n_items);
+        else fmha_fwd_d64_items_combine<false><<<cgrid, 128, 0, stream>>>(a, n_items);
+    } else if (a.num_splits > 1) {
         if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         dim3 cgrid((unsigned)(ntiles * (kRowsPerCta / 128)), 1, 1);
         if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, 128, 0, stream>>>(a, ntiles);
@@ -1267,6 +1323,24 @@ int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int 
     if ((long long)ntiles * num_splits > 0x7fffffffll) return FMHA_ERR_ARG;
     return launch(params, batch, causal != 0, params->seqstart_q != nullptr, total_q, total_k,
                   stream, tiles, ntiles, num_splits, static_cast<float*>(workspace));
+}
+
+size_t fmha_fwd_d64_items_workspace_bytes(int n_items) {
+    if (n_items <= 0) return 0;
+    return (size_t)n_items * kRowsPerCta * (kHeadDim + 1) * sizeof(float);
+}
+
+int fmha_fwd_d64_bf16_items(const FmhaFwdParams* params, int batch, int causal, int total_q,
+                            int total_k, const int32_t* items, int n_items, void* workspace,
+                            size_t workspace_bytes, CUstream_st* stream) {
+    if (params == nullptr || n_items < 0) return FMHA_ERR_ARG;
+    if (n_items == 0) return FMHA_OK;
+    if (items == nullptr || ((uintptr_t)items & 15u) != 0) return FMHA_ERR_ARG;
+    if (workspace == nullptr || ((uintptr_t)workspace & 15u) != 0 ||
+        workspace_bytes < fmha_fwd_d64_items_workspace_bytes(n_items))
+        return FMHA_ERR_ARG;
+    return launch(params, batch, causal != 0, params->seqstart_q != nullptr, total_q, total_k,
+                  stream, nullptr, -1, 1, static_cast<float*>(workspace), items, n_items);
 }
 
 int fmha_fwd_d64_status(CUstream_st* stream) {

@@ -1,11 +1,10 @@
 """Work partitioning of one forward pass across GPUs (and ordering within
 one GPU).
 
-The unit of work is a query block: 256 query rows (two 128-row tiles) of one
-(sequence, head), the work one CTA of the kernel performs.  Its cost is the
-number of 128-key tiles its two row tiles visit (causal blocks near the top
-of a sequence are cheap, blocks at the bottom are expensive) plus a fixed
-per-block overhead.  Blocks are independent -- each reads only its own Q rows
+The unit of work is a query block: 128 query rows of one (sequence, head),
+the work one CTA of the kernel performs.  Its cost is the number of 128-key
+tiles it visits (causal blocks near the top of a sequence are cheap, blocks
+at the bottom are expensive) plus a fixed per-block overhead.  Blocks are independent -- each reads only its own Q rows
 and the K/V of its (sequence, kv head) -- so a partition needs no exchange:
 every rank holds K/V, runs `fmha_fwd_d64_bf16_tiles` on its own list and
 writes disjoint rows of O / LSE.
@@ -98,6 +97,48 @@ def tiles_array(part: Sequence[Block]):
     import numpy as np
 
     return np.asarray([(b[0], b[1]) for b in part], dtype=np.int32).reshape(-1, 2)
+
+
+Item = Tuple[int, int, int, int]  # (b*nhead_q + h, query block, kv_begin, kv_end)
+
+
+def plan_items(part: Sequence[Block], slots: int = 2 * 148,
+               min_chunk: int = 4) -> List[Item]:
+    """Work items for fmha_fwd_d64_bf16_items: a block whose KV range is
+    longer than `chunk` tiles is cut into near-equal consecutive ranges
+    (partial items, merged after the launch); the others stay whole
+    (kv_end = -1, written directly).  Splitting starts only when the
+    heaviest block exceeds the average load of a CTA slot (below that,
+    heaviest-first whole blocks already balance and each split only adds a
+    prologue and a merge); then chunk = total KV tiles / (2 * slots), at
+    least `min_chunk`: about two items per slot, so the heaviest causal
+    blocks no longer set the critical path.  Blocks are listed heaviest
+    piece first (the hardware starts CTAs in list order), a split block's
+    pieces consecutively."""
+    if not part:
+        return []
+    n_kv = [max(0, int(round(b[2] - BLOCK_OVERHEAD))) for b in part]
+    total = sum(n_kv)
+    chunk = max(min_chunk, -(-total // (2 * slots)))
+    if max(n_kv) <= max(chunk, total / slots):
+        return [(b[0], b[1], 0, -1) for b in part]
+    groups = []
+    for b, n in zip(part, n_kv):
+        if n <= chunk:
+            groups.append((n, [(b[0], b[1], 0, -1)]))
+            continue
+        k = -(-n // chunk)
+        edges = [n * i // k for i in range(k + 1)]
+        groups.append((n / k, [(b[0], b[1], edges[i], edges[i + 1]) for i in range(k)]))
+    groups.sort(key=lambda g: -g[0])  # stable: ties keep the head-major order
+    return [it for _, its in groups for it in its]
+
+
+def items_array(items: Sequence[Item]):
+    """int32 [n, 4] array of work items for the C ABI."""
+    import numpy as np
+
+    return np.asarray(items, dtype=np.int32).reshape(-1, 4)
 
 
 def choose_splits(nblocks: int, sms: int = 148, target_waves: float = 2.0,

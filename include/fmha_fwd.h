@@ -145,6 +145,30 @@ int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int 
                                     int ntiles, int num_splits, void* workspace,
                                     size_t workspace_bytes, struct CUstream_st* stream);
 
+/* Split-KV with a KV range per work item, for problems whose heaviest query
+ * blocks would otherwise set the critical path (a strong-scaled shard of a
+ * long causal sequence with few heads).  `items` is a device array of
+ * n_items int4 records (b*nhead_q + h, m, kv_begin, kv_end), 16-byte
+ * aligned, one CTA each, run in list order:
+ *   kv_end <  0 : query block m over its whole key range, O/LSE written
+ *                 directly (as fmha_fwd_d64_bf16_tiles);
+ *   kv_end >= 0 : KV tiles [kv_begin, kv_end) (128 keys each, clipped to the
+ *                 block's causal/sequence end) into partial slot `item` of
+ *                 `workspace`; every run of consecutive partial items naming
+ *                 the same block is merged after the launch, on the same
+ *                 stream, into that block's O/LSE (LSE = log sum exp lse_s,
+ *                 O = sum exp(lse_s - LSE) O_s).  A block's partial items
+ *                 must be consecutive and cover its key range exactly once.
+ * workspace: device memory of at least fmha_fwd_d64_items_workspace_bytes(
+ * n_items) bytes, 16-byte aligned, owned by the caller.  No reference
+ * counterpart (one work group per query tile over its whole key range,
+ * src/fused/pipeline.hpp:286-401). */
+size_t fmha_fwd_d64_items_workspace_bytes(int n_items);
+int fmha_fwd_d64_bf16_items(const FmhaFwdParams* params, int batch, int causal,
+                            int total_q, int total_k, const int32_t* items, int n_items,
+                            void* workspace, size_t workspace_bytes,
+                            struct CUstream_st* stream);
+
 /* Allocation-free variant of fmha_fwd_d64_bf16_tiles.  No counterpart in the
  * reference.  Meant for callers that may not allocate device memory: code
  * running where cudaMalloc is refused or would stall the device (inside a
