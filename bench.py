@@ -219,9 +219,10 @@ def native_arm(args, workload_key):
     workspace = None
     items = None
     if tiles is not None:
-        if args.splits > 0:
+        if not args.items:
             # uniform split-KV (every block cut into `splits` equal KV ranges)
-            splits = args.splits
+            # when this rank's blocks cannot fill the GPU (long causal, few heads)
+            splits = args.splits if args.splits > 0 else shd.choose_splits(tiles.shape[0])
             if splits > 1:
                 workspace = torch.empty(fm.splitkv_workspace_bytes(tiles.shape[0], splits) // 4,
                                         device=dev, dtype=torch.float32)
@@ -420,6 +421,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--splits", type=int, default=0,
                     help="split-KV factor for --shard (0 = automatic)")
+    ap.add_argument("--items", action="store_true",
+                    help="with --shard: per-block split-KV work items (shard.plan_items) "
+                         "instead of uniform splits")
     ap.add_argument("--shard", action="store_true",
                     help="strong scaling: split one problem's query blocks over the ranks")
     ap.add_argument("--traffic", type=float, default=None,

@@ -860,10 +860,13 @@ fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) 
 }
 
 // Work-item combine: block x merges the run of consecutive partial items of
-// one query block that starts at item x (other blocks return at once).
+// one query block that starts at item x (other blocks return at once).  The
+// run length is found with one parallel probe per thread (128 items per
+// pass), not a chain of dependent loads.
 template <bool kVarlen>
 __global__ void __launch_bounds__(128)
 fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
+    __shared__ int run_end;
     const int x = blockIdx.x;
     const int4* items = reinterpret_cast<const int4*>(a.items);
     const int4 it = items[x];
@@ -872,11 +875,22 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
         const int4 prev = items[x - 1];
         if (prev.w >= 0 && prev.x == it.x && prev.y == it.y) return;  // not the run's head
     }
-    int n = 1;
-    while (x + n < n_items) {
-        const int4 nx = items[x + n];
-        if (nx.w < 0 || nx.x != it.x || nx.y != it.y) break;
-        ++n;
+    int n = 0;
+    for (int base = x + 1;; base += 128) {
+        if (threadIdx.x == 0) run_end = n_items;
+        __syncthreads();
+        const int y = base + (int)threadIdx.x;
+        if (y < n_items) {
+            const int4 nx = items[y];
+            if (nx.w < 0 || nx.x != it.x || nx.y != it.y) atomicMin(&run_end, y);
+        }
+        __syncthreads();
+        const int e = run_end;
+        __syncthreads();
+        if (e < base + 128 || base + 128 >= n_items) {
+            n = min(e, n_items) - x;
+            break;
+        }
     }
     merge_row<kVarlen>(a, it.x, it.y, x, n, threadIdx.x);
 }

@@ -15,9 +15,11 @@ pytestmark = []
 
 
 def test_choose_splits():
-    assert shard.choose_splits(314) == 1
+    assert shard.choose_splits(314) == 2
     assert shard.choose_splits(39) == 8
-    assert shard.choose_splits(100) == 3
+    assert shard.choose_splits(79) == 8
+    assert shard.choose_splits(100) == 6
+    assert shard.choose_splits(600) == 1
     assert shard.choose_splits(10000) == 1
 
 
