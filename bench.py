@@ -1,16 +1,18 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 D64 BF16 FMHA forward (driver contract).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl native|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5b] [--impl native|reference]
 
-One step = one forward pass over the workload.  Default workload is
-North-star workload c2 (B4 H16 S2048 non-causal).  Multi-GPU (torchrun, one rank
-per GPU): every rank runs its own shard of a global batch that grows with N
-(weak scaling, no collective on the data path); time = max over ranks.
+One step = one forward pass over the workload.  Default workload is the
+largest single-GPU north-star configuration, c5b (B32 H32 S4096 causal).
+Multi-GPU (torchrun, one rank per GPU): by default the same problem is split
+over the ranks (strong scaling): every rank holds the inputs and computes its
+LPT share of the query blocks, no collective on the data path; time = max
+over ranks.  `--weak` runs an independent copy per rank instead.
 
 `--impl reference` times the reference's own CPU implementation of the path
 (its cpu_ref_verify, compiled from its sources into oracle/_ref) on a bounded
-sample of the same workload, on rank 0 only.
+sample of the same workload, on rank 0 only, with every host core.
 """
 from __future__ import annotations
 
@@ -110,6 +112,9 @@ def reference_arm(args, workload_key):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
+    # torchrun exports OMP_NUM_THREADS=1; the reference's OpenMP runtime reads
+    # it when its library loads, so every host core is requested first.
+    os.environ["OMP_NUM_THREADS"] = str(host_cores())
     import numpy as np
 
     sys.path.insert(0, os.path.join(REPO, "oracle"))
@@ -126,7 +131,8 @@ def reference_arm(args, workload_key):
     line = {
         "metric": METRIC, "value": res["tflops"], "unit": UNIT, "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": res["ms"], "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": res["ms"], "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16 in / fp32 accumulate (CPU)", "data": "synthetic",
         "config": {"workload": w.name, "sample": sample["desc"]},
         "cpu_baseline": {"value": res["tflops"], "unit": UNIT, "cores": res["threads"],
@@ -138,23 +144,43 @@ def reference_arm(args, workload_key):
     return 0
 
 
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def omp_threads() -> int:
+    """Threads the OpenMP runtime of this process will use."""
+    import ctypes
+
+    try:
+        return int(ctypes.CDLL("libgomp.so.1").omp_get_max_threads())
+    except Exception:
+        return int(os.environ.get("OMP_NUM_THREADS", "1"))
+
+
+CPU_SAMPLE_MAC = 1.5e10  # multiply-adds per CPU sample: ~1-20 s on the host
+
+
 def cpu_sample(w):
     """A bounded sample of workload `w` for the reference CPU oracle: every
-    (batch, head) pair, a slice of the query rows, all keys they attend.
-    For non-causal rows the per-row cost is the full workload's, so FLOPs
-    scale exactly; causal samples use the last query rows (full-length
-    rows, the worst case) and count their exact unmasked area."""
+    (batch, head) pair, the last query rows (full-length rows, the most
+    expensive ones), all keys.  The row count is chosen so the sample costs
+    about CPU_SAMPLE_MAC multiply-adds (QK^T + PV).  FLOPs are counted with
+    the metric's convention on the sample's exact (unmasked) area."""
     if w.varlen_seqs:
-        seqs = list(w.varlen_seqs)[:4]
-        b, h, s = len(seqs), w.heads, max(seqs)
-        sq = 256
-        return {"desc": f"varlen first 4 seqs {seqs}, H{h}, 256 query rows each (as Sq=256, Sk=S_b)",
-                "b": 1, "h": h, "sq": sq, "sk": seqs[0], "causal": w.causal,
-                "flops": 4.0 * h * sq * seqs[0] * 64 * (1.0 if not w.causal else (1 - (sq - 1) / (2.0 * seqs[0])))}
+        seqs = list(w.varlen_seqs)
+        s = max(seqs)
+        h = w.heads
+        sq = int(min(256, max(16, CPU_SAMPLE_MAC / (h * s * 64 * 2))))
+        keys = sum(range(s - sq + 1, s + 1)) if w.causal else sq * s
+        return {"desc": f"varlen longest sequence (S={s}), H{h}, its last {sq} query rows",
+                "b": 1, "h": h, "sq": sq, "sk": s, "causal": w.causal,
+                "flops": 4.0 * h * keys * 64}
     b, h, s = w.batch, w.heads, w.seqlen
-    sq = 256 if s >= 256 else s
-    if b * h < 4:
-        sq = min(s, 128)
+    sq = int(min(256, s, max(16, CPU_SAMPLE_MAC / (b * h * s * 64 * 2))))
     flops = 4.0 * b * h * sq * s * 64
     if w.causal:
         # rows i = S-sq..S-1 attend i+1 keys
@@ -181,9 +207,22 @@ def time_cpu_reference(O, sample, steps, warmup):
         if it >= warmup:
             times.append(dt)
     ms = 1000.0 * sum(times) / len(times)
-    # cpu_ref_verify parallelises (b,h) pairs in chunks of 16 (cpu_ref.cpp:84)
-    threads = min(os.cpu_count() or 1, max(1, -(-(b * h) // 16)))
+    # cpu_ref_verify hands out (b,h) pairs in chunks of 16 (cpu_ref.cpp:84),
+    # so at most ceil(B*H/16) of the runtime's threads get work.
+    threads = min(omp_threads(), max(1, -(-(b * h) // 16)))
     return {"ms": ms, "tflops": sample["flops"] / (ms * 1e-3) / 1e12, "threads": threads}
+
+
+def load_traffic(workload_key):
+    """DRAM bytes per launch of the main kernel on this workload, from the
+    committed ncu summary (profiles/ncu_traffic.json), or None."""
+    try:
+        with open(os.path.join(REPO, "profiles", "ncu_traffic.json")) as f:
+            d = json.load(f)
+        e = d.get(workload_key)
+        return (float(e["dram_bytes_per_launch"]), e.get("how", "")) if e else (None, "")
+    except Exception:
+        return None, ""
 
 
 def native_arm(args, workload_key):
@@ -205,16 +244,32 @@ def native_arm(args, workload_key):
     # Weak scaling (default): every rank runs its own copy of the workload on
     # its own data.  --shard (strong scaling): one problem, every rank holds
     # the same inputs and computes its share of the query blocks.
+    if world > 1 and not args.weak:
+        args.shard = True
     q, k, v, cu = make_inputs(w, dev, seed_base=0 if args.shard else 1000 * rank)
     tiles = None
     share = 1.0
+    shard_mode = None
     if args.shard:
         from fmha_native_b200 import shard as shd
 
-        blocks = shd.plan_blocks(w.batch, w.heads, w.seqlen, w.seqlen, w.causal, w.varlen_seqs)
-        part = shd.partition(blocks, world)[rank]
-        tiles = torch.from_numpy(shd.tiles_array(part)).to(dev)
-        share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
+        if not w.varlen_seqs and w.batch % world == 0 and not args.items:
+            # (batch, head) partition: every rank owns a contiguous slice of
+            # the batch -- its own Q/K/V/O, nothing replicated, equal work.
+            shard_mode = "batch"
+            per = w.batch // world
+            sl = slice(rank * per, (rank + 1) * per)
+            q, k, v = q[sl], k[sl], v[sl]
+            share = 1.0 / world
+        else:
+            # query-tile partition (few heads, long causal sequences, varlen):
+            # LPT over all query blocks, K/V replicated on every rank.
+            shard_mode = "tiles"
+            blocks = shd.plan_blocks(w.batch, w.heads, w.seqlen, w.seqlen, w.causal,
+                                     w.varlen_seqs)
+            part = shd.partition(blocks, world)[rank]
+            tiles = torch.from_numpy(shd.tiles_array(part)).to(dev)
+            share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
     splits = 1
     workspace = None
     items = None
@@ -240,8 +295,10 @@ def native_arm(args, workload_key):
         if w.varlen_seqs:
             lse = torch.empty(w.heads, w.tokens(), device=dev, dtype=torch.float32)
         else:
-            lse = torch.empty(w.batch, w.heads, w.seqlen, device=dev, dtype=torch.float32)
-    params, batch, tq, tk = fm.params_from_tensors(q, k, v, o, lse, layout, cu, cu)
+            lse = torch.empty(q.shape[0], w.heads, w.seqlen, device=dev, dtype=torch.float32)
+    max_s = max(w.varlen_seqs) if w.varlen_seqs else None
+    params, batch, tq, tk = fm.params_from_tensors(q, k, v, o, lse, layout, cu, cu,
+                                                   max_seqlen_q=max_s, max_seqlen_k=max_s)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev, dtype=torch.float32)
@@ -301,7 +358,8 @@ def native_arm(args, workload_key):
     achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API, copies inside the timed region
-    e2e = e2e_measure(fm, w, dev, args, tiles, splits, items)
+    e2e = e2e_measure(fm, w, dev, args, tiles, splits, items,
+                      batch_slice=(rank, world) if shard_mode == "batch" else None)
     if world > 1:
         t = torch.tensor([e2e["ms"]], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -312,6 +370,10 @@ def native_arm(args, workload_key):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w)
 
+    traffic, traffic_how = (args.traffic, "--traffic") if args.traffic else load_traffic(
+        args.config)
+    if traffic is not None and world > 1:
+        traffic = traffic * share  # the committed figure is for the whole problem
     if rank == 0:
         alg_bytes = 2 * (q.numel() + k.numel() + v.numel() + o.numel()) + (
             lse.numel() * 4 if lse is not None else 0)
@@ -326,18 +388,19 @@ def native_arm(args, workload_key):
                        "lse": w.lse,
                        "splitkv": (f"per-block: {items.shape[0]} items, "
                                    f"{int((items[:, 3] >= 0).sum().item())} partial"
-                                   if items is not None else splits), "parallelism": (f"LPT query-block shards over {world} GPU(s), K/V replicated, "
-                                       "no collective" if args.shard else
-                                       f"{world} independent replicas (weak scaling), no collective"), "l2": "flushed (256 MiB write) between steps"},
+                                   if items is not None else splits),
+                       "parallelism": parallelism_desc(shard_mode, world),
+                       "l2": "flushed (256 MiB write) between steps"},
             "pct_of_bf16_peak": round(100.0 * (value / world) / peak_tf, 2),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak_tf,
                          "unit": UNIT, "frac": round(achieved / peak_tf, 4),
                          "peak_kind": f"{peak_kind} bf16_tflops (burst)",
-                         "alg_bytes_per_launch": alg_bytes, "traffic": args.traffic},
+                         "alg_bytes_per_launch": alg_bytes, "traffic": traffic,
+                         "traffic_source": traffic_how},
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT,
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                    "ms_per_step": round(e2e["ms"], 4)},
-            "gpu_launches": args.steps,
+                    "ms_per_step": round(e2e["ms"], 4), "mode": e2e["mode"]},
+            "gpu_launches": args.steps * (2 if (splits > 1 or items is not None) else 1),
             "clocks": clocks,
         }
         if cpu is not None:
@@ -348,25 +411,45 @@ def native_arm(args, workload_key):
     return 0
 
 
-def e2e_measure(fm, w, dev, args, tiles=None, splits=1, items=None):
+def parallelism_desc(shard_mode, world):
+    if shard_mode == "batch":
+        return f"(batch, head) shards: contiguous batch slice per GPU over {world} GPU(s), no collective"
+    if shard_mode == "tiles":
+        return f"LPT query-block shards over {world} GPU(s), K/V replicated, no collective"
+    return f"{world} independent replicas (weak scaling), no collective"
+
+
+def e2e_measure(fm, w, dev, args, tiles=None, splits=1, items=None, batch_slice=None):
     """Public API with pinned host buffers: H2D of Q,K,V (and cu_seqlens),
-    the kernel, D2H of O (and LSE) -- all inside CUDA events."""
+    the kernel, D2H of O -- all inside CUDA events on the calling stream.
+    Dense problems go through fmha_fwd_from_host (batch chunks, copies on one
+    stream overlapping the kernel on another); a (batch, head) shard copies
+    only its own batch slice."""
     import torch
     from fmha_native_b200.synth import make_inputs
 
     q, k, v, cu = make_inputs(w, dev, seed_base=77)
+    if batch_slice is not None:
+        r, n = batch_slice
+        per = w.batch // n
+        q, k, v = (t[r * per:(r + 1) * per] for t in (q, k, v))
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hcu = cu.cpu().pin_memory() if cu is not None else None
     ho = torch.empty_like(hq).pin_memory()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     do = torch.zeros_like(q)
     dcu = torch.empty_like(cu) if cu is not None else None
-    hl = None
     stream = torch.cuda.current_stream(dev)
     h2d = 3 * hq.numel() * 2 + (hcu.numel() * 4 if hcu is not None else 0)
     d2h = ho.numel() * 2
+    max_s = max(w.varlen_seqs) if w.varlen_seqs else None
+    pipelined = tiles is None and items is None and not w.varlen_seqs
 
     def one():
+        if pipelined:
+            fm.fmha_fwd_from_host(hq, hk, hv, causal=w.causal, layout=w.layout, out=ho,
+                                  chunks=min(8, q.shape[0]), device=dev)
+            return
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
@@ -375,7 +458,8 @@ def e2e_measure(fm, w, dev, args, tiles=None, splits=1, items=None):
         o = fm.fmha_fwd(dq, dk, dv, causal=w.causal, return_lse=False, layout=w.layout,
                         cu_seqlens_q=dcu, cu_seqlens_k=dcu, stream=stream.cuda_stream,
                         out=do, tiles=None if items is not None else tiles,
-                        num_splits=splits, items=items)
+                        num_splits=splits, items=items, max_seqlen_q=max_s,
+                        max_seqlen_k=max_s)
         ho.copy_(o, non_blocking=True)
 
     for _ in range(2):
@@ -388,7 +472,8 @@ def e2e_measure(fm, w, dev, args, tiles=None, splits=1, items=None):
         one()
     e.record(stream)
     torch.cuda.synchronize()
-    return {"ms": s.elapsed_time(e) / n, "h2d": h2d, "d2h": d2h}
+    return {"ms": s.elapsed_time(e) / n, "h2d": h2d, "d2h": d2h,
+            "mode": "chunked overlap (fmha_fwd_from_host)" if pipelined else "serial"}
 
 
 def cpu_baseline(w):
@@ -416,7 +501,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2")
+    ap.add_argument("--config", default="c5b",
+                    help="north-star workload (fmha_native_b200.synth.WORKLOADS)")
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--splits", type=int, default=0,
@@ -425,7 +511,9 @@ def main():
                     help="with --shard: per-block split-KV work items (shard.plan_items) "
                          "instead of uniform splits")
     ap.add_argument("--shard", action="store_true",
-                    help="strong scaling: split one problem's query blocks over the ranks")
+                    help="strong scaling: split one problem over the ranks (default for N>1)")
+    ap.add_argument("--weak", action="store_true",
+                    help="N>1: every rank runs its own copy of the workload (weak scaling)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch to report in roofline.traffic")
     args = ap.parse_args()

@@ -53,6 +53,7 @@ ENTRY_POINTS = (
     "fmha_fwd_d64_items_workspace_bytes",
     "fmha_fwd_d64_status",
     "fmha_fwd_d64_set_wait_limit_ns",
+    "fmha_fwd_d64_set_max_ctas",
     "fmha_fwd_d64_release",
     "fmha_fwd_d64_error_string",
 )
@@ -128,6 +129,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fmha_fwd_d64_status.restype = ctypes.c_int
     lib.fmha_fwd_d64_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
     lib.fmha_fwd_d64_set_wait_limit_ns.restype = None
+    lib.fmha_fwd_d64_set_max_ctas.argtypes = [ctypes.c_int]
+    lib.fmha_fwd_d64_set_max_ctas.restype = None
     lib.fmha_fwd_d64_release.argtypes = []
     lib.fmha_fwd_d64_release.restype = None
     lib.fmha_fwd_d64_error_string.argtypes = [ctypes.c_int]
@@ -248,11 +251,15 @@ def status(stream: int = 0) -> int:
 
 
 def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
-                        seqstart_q=None, seqstart_k=None, scale: Optional[float] = None):
+                        seqstart_q=None, seqstart_k=None, scale: Optional[float] = None,
+                        max_seqlen_q: Optional[int] = None, max_seqlen_k: Optional[int] = None):
     """Build FmhaFwdParams from torch CUDA tensors.
 
     Dense layouts: "bshd" ([B,S,H,D]) or "bhsd" ([B,H,S,D]).
-    Varlen layouts: "thd" ([total,H,D]) or "htd" ([H,total,D]).
+    Varlen layouts: "thd" ([total,H,D]) or "htd" ([H,total,D]); the longest
+    sequence lengths go into seqlen_q/seqlen_k (the reference's varlen
+    convention).  Pass max_seqlen_q/max_seqlen_k when known: otherwise they
+    are read from the device prefix sums, which synchronises the stream.
     Returns (params, batch, total_q, total_k).
     """
     p = FmhaFwdParams()
@@ -276,10 +283,13 @@ def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
         t_ax, h_ax = (0, 1) if layout == "thd" else (1, 0)
         batch = seqstart_q.numel() - 1
         total_q, total_k = q.shape[t_ax], k.shape[t_ax]
-        sq = seqstart_q.to("cpu")
-        sk = seqstart_k.to("cpu")
-        p.seqlen_q = int((sq[1:] - sq[:-1]).max()) if batch > 0 else 0
-        p.seqlen_k = int((sk[1:] - sk[:-1]).max()) if batch > 0 else 0
+        if max_seqlen_q is None or max_seqlen_k is None:
+            sq = seqstart_q.to("cpu")
+            sk = seqstart_k.to("cpu")
+            max_seqlen_q = int((sq[1:] - sq[:-1]).max()) if batch > 0 else 0
+            max_seqlen_k = int((sk[1:] - sk[:-1]).max()) if batch > 0 else 0
+        p.seqlen_q = int(max_seqlen_q)
+        p.seqlen_k = int(max_seqlen_k)
         p.nhead_q, p.nhead_k = q.shape[h_ax], k.shape[h_ax]
         for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
             st = t.stride()
@@ -294,7 +304,8 @@ def params_from_tensors(q, k, v, o, lse=None, layout: str = "bshd",
 
 def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: str = "bshd",
              cu_seqlens_q=None, cu_seqlens_k=None, out=None, lse_out=None, stream=None,
-             tiles=None, num_splits: int = 1, workspace=None, items=None):
+             tiles=None, num_splits: int = 1, workspace=None, items=None,
+             max_seqlen_q: Optional[int] = None, max_seqlen_k: Optional[int] = None):
     """O = softmax(Q K^T / 8) V on the B200 kernel (head_dim 64, bf16).
 
     Dense: q [B,Sq,Hq,64] ("bshd") or [B,Hq,Sq,64] ("bhsd"); varlen: q
@@ -308,6 +319,8 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
     `items`: optional device int32 [n, 4] work-item list with per-item KV
     ranges (fmha_native_b200.shard.plan_items); `workspace` then holds
     items_workspace_bytes(n) bytes (allocated here when omitted).
+    `max_seqlen_q/k` (varlen): the longest sequence lengths, if known; else
+    they are read from cu_seqlens (a stream synchronisation).
     """
     import torch
 
@@ -328,7 +341,9 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
             s_ax, h_ax = (1, 2) if layout == "bshd" else (2, 1)
             lse = torch.empty(q.shape[0], q.shape[h_ax], q.shape[s_ax], device=q.device,
                               dtype=torch.float32)
-    params, batch, tq, tk = params_from_tensors(q, k, v, o, lse, layout, cu_seqlens_q, cu_seqlens_k)
+    params, batch, tq, tk = params_from_tensors(q, k, v, o, lse, layout, cu_seqlens_q,
+                                                cu_seqlens_k, max_seqlen_q=max_seqlen_q,
+                                                max_seqlen_k=max_seqlen_k)
     s = stream if stream is not None else torch.cuda.current_stream(q.device).cuda_stream
     if items is not None:
         nbytes = items_workspace_bytes(items.shape[0])
@@ -352,3 +367,62 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
     else:
         _check(call_entry(params, batch, causal, varlen, tq, tk, s), "fmha_fwd")
     return (o, lse) if return_lse else o
+
+
+def fmha_fwd_from_host(q, k, v, causal: bool = False, layout: str = "bshd", out=None,
+                       chunks: int = 4, device=None):
+    """O = attention(Q, K, V) for dense inputs that live in (pinned) HOST
+    memory: the batch is cut into `chunks` slices whose host->device copies,
+    kernel launches and device->host copy of O run on two streams, so the
+    PCIe transfers of one slice overlap the kernel of the previous one.
+    Returns the host tensor `out` (allocated pinned when omitted).  The
+    caller's current stream is ordered after the last copy: synchronise it
+    before reading `out`.  Device staging buffers are cached per shape."""
+    import torch
+
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if layout not in ("bshd", "bhsd"):
+        raise FmhaError(FMHA_ERR_ARG, "fmha_fwd_from_host takes dense layouts")
+    B = q.shape[0]
+    chunks = max(1, min(chunks, B))
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    key = (tuple(q.shape), tuple(k.shape), dev.index)
+    st = _host_state.get(key)
+    if st is None:
+        st = {"dq": torch.empty(q.shape, dtype=q.dtype, device=dev),
+              "dk": torch.empty(k.shape, dtype=k.dtype, device=dev),
+              "dv": torch.empty(v.shape, dtype=v.dtype, device=dev),
+              "do": torch.empty(q.shape, dtype=q.dtype, device=dev),
+              "copy": torch.cuda.Stream(dev), "comp": torch.cuda.Stream(dev)}
+        _host_state[key] = st
+    cur = torch.cuda.current_stream(dev)
+    copy, comp = st["copy"], st["comp"]
+    copy.wait_stream(cur)
+    comp.wait_stream(cur)
+    bounds = [B * i // chunks for i in range(chunks + 1)]
+    done = []
+    for i in range(chunks):
+        b0, b1 = bounds[i], bounds[i + 1]
+        if b0 == b1:
+            continue
+        with torch.cuda.stream(copy):
+            for name, h in (("dq", q), ("dk", k), ("dv", v)):
+                st[name][b0:b1].copy_(h[b0:b1], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+        comp.wait_event(ev)
+        fmha_fwd(st["dq"][b0:b1], st["dk"][b0:b1], st["dv"][b0:b1], causal=causal,
+                 layout=layout, out=st["do"][b0:b1], stream=comp.cuda_stream)
+        ev2 = torch.cuda.Event()
+        ev2.record(comp)
+        done.append((b0, b1, ev2))
+    with torch.cuda.stream(copy):
+        for b0, b1, ev2 in done:
+            copy.wait_event(ev2)
+            out[b0:b1].copy_(st["do"][b0:b1], non_blocking=True)
+    cur.wait_stream(copy)
+    return out
+
+
+_host_state: dict = {}

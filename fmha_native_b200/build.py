@@ -77,7 +77,27 @@ def build_cli(force: bool = False) -> str:
     return CLI_PATH
 
 
+TEST_SRC = os.path.join(REPO_DIR, "tests", "native", "unit_kernels.cu")
+TEST_LIB = os.path.join(REPO_DIR, "tests", "native", "libfmha_unit.so")
+
+
+def build_test_lib(force: bool = False) -> str | None:
+    """Test-only library exposing single device helpers of the kernel
+    (tests/native/unit_kernels.cu); skipped when the tests tree is absent."""
+    if not os.path.exists(TEST_SRC):
+        return None
+    deps = [TEST_SRC, os.path.join(CSRC, "sm100_ptx.cuh")]
+    if not force and not _stale(TEST_LIB, deps):
+        return TEST_LIB
+    subprocess.run([nvcc_path(), *ARCH_FLAGS, "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
+                    "-shared", "--cudart", "static", TEST_SRC, "-o", TEST_LIB + ".tmp"],
+                   check=True)
+    os.replace(TEST_LIB + ".tmp", TEST_LIB)
+    return TEST_LIB
+
+
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose="-v" in sys.argv)
     build_cli(force="--force" in sys.argv)
+    build_test_lib(force="--force" in sys.argv)
     print(LIB_PATH)

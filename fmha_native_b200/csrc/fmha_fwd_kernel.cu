@@ -1,33 +1,36 @@
 // fmha_fwd_kernel.cu -- B200 (sm_100a) head-dim-64 BF16 fused attention
 // forward, and the C-ABI launchers declared in include/fmha_fwd.h.
 //
-// One CTA owns one 128-row query tile of one (batch, head) and walks the
-// key/value sequence in 128-key tiles; two CTAs share each SM, each with its
-// own pipeline.  The CTA is warp specialised:
+// A persistent CTA loops over 128-row query tiles of (batch, head) pairs
+// (work items dealt out in rounds, alternating direction) and walks each
+// tile's key/value sequence in 128-key tiles; two CTAs share each SM, each
+// with its own pipeline.  The CTA is warp specialised:
 //
-//   warps 0-3  softmax          : one query row per thread (TMEM lane = row)
-//   warp  4    TMA producer     : Q once, then K_j / V_j into a 4-slot ring
-//   warp  5    MMA issuer       : one elected lane issues every tcgen05.mma;
-//                                 the warp also owns the TMEM allocation
-//   warps 6-7  idle             : complete the control warpgroup for setmaxnreg
+//   warps 0-3  softmax + epilogue : one query row per thread (TMEM lane = row)
+//   warp  4    TMA producer       : Q of the current and next tile (double
+//                                   buffer), K_j / V_j into a 4-slot ring
+//   warp  5    MMA issuer         : one elected lane issues every tcgen05.mma;
+//                                   the warp also owns the TMEM allocation
+//   warps 6-7  idle               : complete the control warpgroup for setmaxnreg
 //
 // Tensor memory (256 columns x 128 lanes per CTA; two CTAs fill the SM):
 //   [  0,128) S = Q K^T (fp32)
 //   [128,192) O accumulator (fp32)
 //   [192,256) P (bf16x2)
 //
-// Per KV tile j the schedule is
-//   MMA : S = Q K_j^T -> commit(s_full)
+// The pipeline is one flat stream of KV steps g across the CTA's tiles:
+//   MMA : S(g) = Q K^T -> commit(s_full)
 //   SM  : S -> registers -> arrive(s_free) -> mask, row max, (lazy) rescale
-//         of O -> P = exp2(S*scale - m*scale) -> wait(pv_done of j-1) ->
+//         of O -> P = exp2(S*scale - m*scale) -> wait(pv_done(g-1)) ->
 //         bf16 P into TMEM -> arrive(p_full)
-//   MMA : S = Q K_{j+1}^T as soon as s_free arrives, then O += P V_j ->
-//         commit(pv_done)
-// tcgen05 MMAs issued by one thread execute in order, so pv_done(j-1) also
+//   MMA : S(g+1) as soon as s_free arrives (also when g+1 starts the next
+//         tile), then O += P(g) V(g) -> commit(pv_done)
+//   SM  : after a tile's last step: wait(pv_done), O -> registers ->
+//         arrive(o_free) -> O/l and LSE to global memory; the MMA warp starts
+//         the next tile's first P V only after o_free.
+// tcgen05 MMAs issued by one thread execute in order, so pv_done(g-1) also
 // proves every earlier MMA finished, which is what makes the softmax-side O
-// rescale race free.  (Build flag FMHA_TILES_PER_CTA=2 keeps the older
-// layout: one CTA per SM with two query tiles sharing one producer and MMA
-// warp.)
+// rescale race free.
 //
 // Reference semantics followed (poyenc/fmha_native):
 //   grid decode + causal heavy-first order ... src/fused/kernel.cpp:55-99
@@ -63,47 +66,25 @@ namespace {
 constexpr int kBlockM = 128;            // rows per query tile
 constexpr int kBlockN = 128;            // keys per KV tile
 constexpr int kHeadDim = 64;
-// Query tiles per CTA.  With 1, each CTA (128 query rows, 256 threads, 256
-// TMEM columns, ~80 KB shared memory) runs two-per-SM, fully independent of
-// its neighbour; with 2, one CTA owns both tiles of an SM.
-#ifndef FMHA_TILES_PER_CTA
-#define FMHA_TILES_PER_CTA 1
-#endif
-constexpr int kTilesPerCta = FMHA_TILES_PER_CTA;
-constexpr int kRowsPerCta = kBlockM * kTilesPerCta;
-constexpr int kCtasPerSm = kTilesPerCta == 1 ? 2 : 1;
-#ifndef FMHA_STAGES
-#define FMHA_STAGES (kTilesPerCta == 1 ? 4 : 6)
-#endif
-constexpr int kStages = FMHA_STAGES;    // K/V ring slots (K_j, V_j alternate)
+constexpr int kCtasPerSm = 2;           // two independent persistent CTAs per SM
+constexpr int kStages = 4;              // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
-constexpr int kWarpsPerTile = 4;   // softmax warps per query tile: one thread per row
-constexpr int kSoftmaxWarps = kWarpsPerTile * kTilesPerCta;
-constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax groups + control group
+constexpr int kSoftmaxWarps = 4;        // one thread per query row
+constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax group + control group
 // Register split (setmaxnreg): the CTA launches with kThreads x kLaunchRegs
-// registers; each softmax group takes kRegsSoftmax, the producer/MMA group
-// kRegsControl: 128 * (kTilesPerCta * kRegsSoftmax + kRegsControl) <=
-// kThreads * kLaunchRegs  (2 tiles: 128*(2*208+88) <= 384*168;
-// 1 tile: 128*(192+64) <= 256*128; 200/56 spilled in the control warps).
-#ifndef FMHA_REGS_SOFTMAX
-#define FMHA_REGS_SOFTMAX (kTilesPerCta == 1 ? 192 : 208)
-#endif
-#ifndef FMHA_REGS_CONTROL
-#define FMHA_REGS_CONTROL (kTilesPerCta == 1 ? 64 : 88)
-#endif
-constexpr int kRegsSoftmax = FMHA_REGS_SOFTMAX;
-constexpr int kRegsControl = FMHA_REGS_CONTROL;
-constexpr int kLaunchRegs = kTilesPerCta == 1 ? 128 : 168;
-static_assert(32 * kSoftmaxWarps * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs,
+// registers; the softmax group takes kRegsSoftmax, the producer/MMA group
+// kRegsControl: 128 * (192 + 64) <= 256 * 128.
+constexpr int kRegsSoftmax = 192;
+constexpr int kRegsControl = 64;
+constexpr int kLaunchRegs = 128;
+static_assert(128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs,
               "setmaxnreg split exceeds the launch register pool");
 constexpr int kWarpLoad = kSoftmaxWarps;
 constexpr int kWarpMma = kSoftmaxWarps + 1;
-constexpr uint32_t kTmemCols = 256 * kTilesPerCta;
-__host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i (fp32)
-__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * kTilesPerCta + i * 64u; }  // O_i
-__host__ __device__ constexpr uint32_t col_p(int i) {  // P_i (bf16x2)
-    return 192u * kTilesPerCta + i * 64u;
-}
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColS = 0;    // S = Q K^T (fp32), 128 columns
+constexpr uint32_t kColO = 128;  // O accumulator (fp32), 64 columns
+constexpr uint32_t kColP = 192;  // P (bf16x2), 64 columns
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
@@ -142,7 +123,7 @@ struct KernelArgs {
     int* err_word;
     unsigned long long wait_limit_ns;
     int stall_inject;          // test hook: producer withholds the first V tile
-    unsigned long long* trace; // FMHA_TRACE builds: per-event clock64 of CTA (0,0)
+    int n_work;                // work items of the launch (CTAs loop over them)
     const int32_t* tiles;      // optional work list of (b*nhead_q+h, query block)
     int m_blocks;              // query blocks per (batch, head) in a full launch
     int head_group;            // (batch, head) pairs per L2 group of the launch order
@@ -153,29 +134,18 @@ struct KernelArgs {
     float* part_lse;           // split-KV partial LSE (natural log) [item][128]
 };
 
-// Pipeline event timestamps (diagnostic builds only, -DFMHA_TRACE): slot
-// 0/1 = softmax group 0/1 (thread 0), 2 = MMA issuer; 8 events per KV tile.
-#ifdef FMHA_TRACE
-#define TRACE_EV(slot, j, ev)                                                          \
-    do {                                                                               \
-        if (a.trace && blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64)                 \
-            a.trace[((slot) * 64 + (j)) * 8 + (ev)] = clock64();                       \
-    } while (0)
-#else
-#define TRACE_EV(slot, j, ev) do { } while (0)
-#endif
-
 struct alignas(1024) SharedStorage {
-    uint8_t q[kTilesPerCta][kTileBytes];
+    uint8_t q[2][kTileBytes];      // Q of the current and the next query tile
     uint8_t kv[kStages][kTileBytes];
-    uint64_t bar_q[kTilesPerCta];
+    uint64_t bar_qfull[2];
+    uint64_t bar_qempty[2];        // Q buffer's last S issued and done (MMA commit)
     uint64_t bar_full[kStages];
     uint64_t bar_empty[kStages];
-    uint64_t bar_s[kTilesPerCta];      // S_i written (MMA commit)
-    uint64_t bar_sfree[kTilesPerCta];  // S_i read into registers (128 arrivals)
-    uint64_t bar_p[kTilesPerCta];      // P_i written, O_i rescaled (128 arrivals)
-    uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
-    uint64_t bar_o[kTilesPerCta];
+    uint64_t bar_s;                // S written (MMA commit)
+    uint64_t bar_sfree;            // S read into registers (128 arrivals)
+    uint64_t bar_p;                // P written, O rescaled (128 arrivals)
+    uint64_t bar_pv;               // O += P V done (MMA commit)
+    uint64_t bar_ofree;            // final O of a tile read out (128 arrivals)
     uint64_t bar_drain;
     uint32_t tmem_base;
     int abort_flag;
@@ -211,47 +181,55 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const
 }
 
 struct TileWork {
-    int n_kv[kTilesPerCta];     // KV tiles each query tile walks (from j0)
+    int n;                      // KV tiles the query tile walks (from j0)
     int j0;                     // first KV tile (split-KV ranges start past 0)
-    int row0;                   // first query row of the CTA (sequence-local)
+    int row0;                   // first query row of the tile (sequence-local)
     int seqlen_q, seqlen_k;
     int off_q, off_k;           // varlen packed-row offsets
     int b, h, kvh;
+    int x;                      // work-item index (split-KV workspace slot)
     bool partial;               // split-KV item: partial O/LSE into the workspace
 };
 
+// Work item x of the launch -> query tile and KV range.  Returns false for an
+// item that computes nothing (a query block past the end of its sequence,
+// or a malformed work-list entry, which is skipped without any access).
 template <bool kCausal, bool kVarlen>
-__device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
+__device__ __forceinline__ bool decode_work(const KernelArgs& a, int x, TileWork& w) {
     int hb, mblk;
     int split = 0;
     int kv_begin = 0, kv_end = -1;  // work items: explicit KV-tile range (end < 0: all)
     if (a.items != nullptr) {
-        const int4 it = reinterpret_cast<const int4*>(a.items)[blockIdx.x];
+        const int4 it = reinterpret_cast<const int4*>(a.items)[x];
         hb = it.x;
         mblk = it.y;
         kv_begin = it.z;
         kv_end = it.w;
+        if (kv_end >= 0 && (kv_begin < 0 || kv_begin > kv_end)) return false;
     } else if (a.tiles != nullptr) {
         // Caller-supplied work list: (batch*nhead_q + head, query block); in
         // split-KV mode every entry expands into num_splits KV ranges.
-        const int x = a.num_splits > 1 ? (int)blockIdx.x / a.num_splits : (int)blockIdx.x;
-        if (a.num_splits > 1) split = (int)blockIdx.x % a.num_splits;
-        hb = a.tiles[2 * x];
-        mblk = a.tiles[2 * x + 1];
+        const int e = a.num_splits > 1 ? x / a.num_splits : x;
+        if (a.num_splits > 1) split = x - e * a.num_splits;
+        hb = a.tiles[2 * e];
+        mblk = a.tiles[2 * e + 1];
     } else {
         // Launch order: (batch, head) pairs in groups of head_group whose K/V
         // fit in L2 together; inside a group causal blocks go heaviest first
         // across all its heads (src/fused/kernel.cpp:73,96), so the group's
         // K/V is read from HBM about once.
         const int mb = a.m_blocks;
-        const int lin = blockIdx.x;
-        const int g = lin / (a.head_group * mb);
-        const int r = lin - g * a.head_group * mb;
+        const int g = x / (a.head_group * mb);
+        const int r = x - g * a.head_group * mb;
         const int gs = min(a.head_group, a.num_hb - g * a.head_group);
         hb = g * a.head_group + r % gs;
         const int mrank = r / gs;
         mblk = kCausal ? mb - 1 - mrank : mrank;
     }
+    // A list entry naming no (batch, head) of the problem, or a negative or
+    // out-of-range query block, is skipped before any address is formed.
+    if (hb < 0 || hb >= a.num_hb || mblk < 0 || mblk >= a.m_blocks) return false;
+    w.x = x;
     w.h = hb % a.nhead_q;
     w.b = hb / a.nhead_q;
     w.kvh = w.h / (a.nhead_q / a.nhead_k);
@@ -260,49 +238,51 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
         w.off_k = a.seqstart_k[w.b];
         w.seqlen_q = a.seqstart_q[w.b + 1] - w.off_q;
         w.seqlen_k = a.seqstart_k[w.b + 1] - w.off_k;
+        if (w.off_q < 0 || w.off_k < 0 || w.seqlen_q < 0 || w.seqlen_k < 0 ||
+            w.off_q + w.seqlen_q > a.total_q)
+            return false;
     } else {
         w.off_q = 0;
         w.off_k = 0;
         w.seqlen_q = a.seqlen_q;
         w.seqlen_k = a.seqlen_k;
     }
-    w.row0 = mblk * kRowsPerCta;
+    w.row0 = mblk * kBlockM;
     if (w.row0 >= w.seqlen_q) return false;
     const int shift = w.seqlen_k - w.seqlen_q;  // bottom-right causal alignment
-#pragma unroll
-    for (int i = 0; i < kTilesPerCta; ++i) {
-        const int r0 = w.row0 + i * kBlockM;
-        if (r0 >= w.seqlen_q) {
-            w.n_kv[i] = 0;
-            continue;
-        }
-        int kv_end = w.seqlen_k;
-        if (kCausal) {
-            const int r_last = min(r0 + kBlockM - 1, w.seqlen_q - 1);
-            kv_end = min(w.seqlen_k, r_last + shift + 1);
-        }
-        w.n_kv[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+    int kend = w.seqlen_k;
+    if (kCausal) {
+        const int r_last = min(w.row0 + kBlockM - 1, w.seqlen_q - 1);
+        kend = min(w.seqlen_k, r_last + shift + 1);
     }
+    w.n = kend > 0 ? (kend + kBlockN - 1) / kBlockN : 0;
     w.j0 = 0;
     w.partial = a.num_splits > 1 || (a.items != nullptr && kv_end >= 0);
     if (a.items != nullptr && kv_end >= 0) {
-        const int jb = max(0, kv_begin);
-#pragma unroll
-        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], kv_end) - jb);
-        w.j0 = jb;
+        w.n = max(0, min(w.n, kv_end) - kv_begin);
+        w.j0 = kv_begin;
     } else if (a.num_splits > 1) {
-        // KV range of this split: an equal share of the longer tile's range.
-        int n_all = 0;
-#pragma unroll
-        for (int i = 0; i < kTilesPerCta; ++i) n_all = max(n_all, w.n_kv[i]);
-        const int chunk = (n_all + a.num_splits - 1) / a.num_splits;
+        // KV range of this split: an equal share of the tile's range.
+        const int chunk = (w.n + a.num_splits - 1) / a.num_splits;
         const int jb = split * chunk;
-        const int je = min(n_all, jb + chunk);
+        const int je = min(w.n, jb + chunk);
         w.j0 = jb;
-#pragma unroll
-        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], je) - jb);
+        w.n = max(0, je - jb);
     }
     return true;
+}
+
+// k-th work item of this CTA: items are dealt out in rounds of gridDim.x,
+// alternately in CTA order and in reverse ("snake"), so a list sorted
+// heaviest first spreads its heavy and light items evenly over the CTAs.
+// Returns -1 past the end of the list, -2 for a hole in the last round.
+__device__ __forceinline__ int work_index(const KernelArgs& a, int k) {
+    const int g = (int)gridDim.x;
+    const long long base = (long long)k * g;
+    if (base >= a.n_work) return -1;
+    const int c = (int)blockIdx.x;
+    const long long x = base + ((k & 1) ? (g - 1 - c) : c);
+    return x < a.n_work ? (int)x : -2;
 }
 
 template <bool kVarlen>
@@ -319,6 +299,78 @@ __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* t
     }
 }
 
+// Output of one query row: O * (1/l) rounded to bf16 and the LSE (dense or
+// varlen layouts), or for a split-KV item the normalised fp32 partial O and
+// its LSE in the workspace.  `o` holds the row's 64 fp32 accumulator columns
+// (zeros when the tile visited no key: the row is O = 0, LSE = -inf,
+// src/fused/pipeline.hpp:207-222).
+template <bool kVarlen>
+__device__ __forceinline__ void store_row(const KernelArgs& a, const TileWork& w, int t,
+                                          const uint32_t (&o)[2][32], bool any_key, float m_run,
+                                          float l_run) {
+    const int row = w.row0 + t;
+    const float inv_l = (any_key && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+    const float lse = (any_key && l_run > 0.0f)
+                          ? (__log2f(l_run) + m_use * a.scale - kPLog2Bias) * 0.69314718055994531f
+                          : -INFINITY;
+    if (w.partial) {
+        const size_t prow = (size_t)w.x * kBlockM + t;
+        float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int col = c * 4 + e;
+                v[e] = __uint_as_float(o[col >> 5][col & 31]) * inv_l;
+            }
+            dst[c] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        a.part_lse[prow] = lse;
+        return;
+    }
+    if (row >= w.seqlen_q) return;
+    uint16_t* orow;
+    if constexpr (kVarlen) {
+        orow = a.o + (long long)w.h * a.nhead_stride_o + (long long)(w.off_q + row) * a.stride_o;
+    } else {
+        orow = a.o + (long long)w.b * a.batch_stride_o + (long long)w.h * a.nhead_stride_o +
+               (long long)row * a.stride_o;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int col = c * 8 + e * 2;
+            const float v0 = __uint_as_float(o[col >> 5][col & 31]) * inv_l;
+            const float v1 = __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l;
+#ifdef FMHA_O_ROUND_TRUNC
+            pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
+#else
+            pk[e] = pack_bf16_rne(v0, v1);
+#endif
+        }
+        dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    if (a.lse != nullptr) {
+        long long idx;
+        if constexpr (kVarlen) {
+            idx = (long long)w.h * a.total_q + w.off_q + row;
+        } else {
+            idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
+        }
+        a.lse[idx] = lse;
+    }
+}
+
+// Persistent CTA: loops over the work items work_index(k), k = 0, 1, ...
+// Every role walks the same item sequence; the pipeline runs on as one flat
+// stream of KV steps across query tiles (step counter g), so the first S of
+// the next tile is computed while the softmax finishes the current one, and
+// the next tile's Q is loaded (double buffer) while the current one runs.
 template <bool kCausal, bool kVarlen>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
@@ -326,22 +378,20 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     SharedStorage& sm = *reinterpret_cast<SharedStorage*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-    TileWork w;
-    if (!decode_work<kCausal, kVarlen>(a, w)) return;  // CTA-uniform early out
-
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     volatile int* abort_flag = &sm.abort_flag;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kTilesPerCta; ++i) {
-            mbar_init(smem_u32(&sm.bar_q[i]), 1);
-            mbar_init(smem_u32(&sm.bar_s[i]), 1);
-            mbar_init(smem_u32(&sm.bar_sfree[i]), 32 * kWarpsPerTile);
-            mbar_init(smem_u32(&sm.bar_p[i]), 32 * kWarpsPerTile);
-            mbar_init(smem_u32(&sm.bar_pv[i]), 1);
-            mbar_init(smem_u32(&sm.bar_o[i]), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&sm.bar_qfull[b]), 1);
+            mbar_init(smem_u32(&sm.bar_qempty[b]), 1);
         }
+        mbar_init(smem_u32(&sm.bar_s), 1);
+        mbar_init(smem_u32(&sm.bar_sfree), 128);
+        mbar_init(smem_u32(&sm.bar_p), 128);
+        mbar_init(smem_u32(&sm.bar_pv), 1);
+        mbar_init(smem_u32(&sm.bar_ofree), 128);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&sm.bar_full[s]), 1);
             mbar_init(smem_u32(&sm.bar_empty[s]), 1);
@@ -359,12 +409,17 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    // Per-tile KV counts as scalars (a runtime-indexed array would live in
-    // local memory).
-    const int n_kv0 = w.n_kv[0];
-    const int n_kv1 = kTilesPerCta > 1 ? w.n_kv[kTilesPerCta - 1] : 0;
-    auto n_kv = [n_kv0, n_kv1](int i) { return i == 0 ? n_kv0 : n_kv1; };
-    const int n_max = max(n_kv0, n_kv1);
+    // Next item of this CTA with at least one KV tile, from round *k on.
+    auto next_tile = [&](int& k, TileWork& w) -> bool {
+        for (;; ++k) {
+            const int x = work_index(a, k);
+            if (x == -1) return false;
+            if (x >= 0 && decode_work<kCausal, kVarlen>(a, x, w) && w.n > 0) {
+                ++k;
+                return true;
+            }
+        }
+    };
 
     if (warp >= kSoftmaxWarps) {
     regs_dec<kRegsControl>();
@@ -376,46 +431,66 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tma_prefetch_desc(&a.tm_v);
             const uint64_t pol_q = l2_policy_evict_first();
             const uint64_t pol_kv = l2_policy_evict_last();
-            const int qbatch = kVarlen ? 0 : w.b;
-            for (int i = 0; i < kTilesPerCta; ++i) {
-                if (n_kv(i) == 0) continue;
-                const uint32_t bar = smem_u32(&sm.bar_q[i]);
-                mbar_arrive_expect_tx(bar, kTileBytes);
-                tma_load_rows<kVarlen>(smem_u32(sm.q[i]), &a.tm_q, bar,
-                                       w.off_q + w.row0 + i * kBlockM, w.h, qbatch, pol_q);
-            }
-            int issued = 0;  // loads issued into the ring
+            int q_issued = 0;  // Q loads issued (tile count)
+            int issued = 0;    // K/V loads issued into the ring
             bool ok = true;
-            const int n_loads = 2 * n_max;
-            for (int idx = 0; idx < n_loads; ++idx) {
-                const int slot = idx % kStages;
-                const uint32_t use = idx / kStages;
-                if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag, a,
-                                kErrTimeoutLoad)) {
-                    ok = false;
-                    break;
-                }
-                if (a.stall_inject && idx == 1) {
-                    // Test hook: never deliver V_0, so the MMA warp's wait runs
-                    // out and the abort path is exercised without any fault.
-                    continue;
-                }
-                const uint32_t bar = smem_u32(&sm.bar_full[slot]);
+            auto issue_q = [&](const TileWork& w) -> bool {
+                const int b = q_issued & 1;
+                if (q_issued >= 2 &&
+                    !wait_phase(smem_u32(&sm.bar_qempty[b]), ((q_issued - 2) >> 1) & 1,
+                                abort_flag, a, kErrTimeoutLoad))
+                    return false;
+                const uint32_t bar = smem_u32(&sm.bar_qfull[b]);
                 mbar_arrive_expect_tx(bar, kTileBytes);
-                const CUtensorMap* tm = (idx & 1) ? &a.tm_v : &a.tm_k;
-                tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), tm, bar,
-                                       w.off_k + (w.j0 + (idx >> 1)) * kBlockN, w.kvh,
-                                       kVarlen ? 0 : w.b, pol_kv);
-                issued = idx + 1;
+                tma_load_rows<kVarlen>(smem_u32(sm.q[b]), &a.tm_q, bar, w.off_q + w.row0, w.h,
+                                       kVarlen ? 0 : w.b, pol_q);
+                ++q_issued;
+                return true;
+            };
+            int k = 0;
+            TileWork cur, nxt;
+            bool have_cur = next_tile(k, cur);
+            if (have_cur) ok = issue_q(cur);
+            int gstep = 0;  // flat KV step counter (for the stall test hook)
+            while (have_cur && ok) {
+                const bool have_nxt = next_tile(k, nxt);
+                for (int j = 0; j < cur.n && ok; ++j, ++gstep) {
+                    for (int kv = 0; kv < 2; ++kv) {
+                        const int idx = issued;
+                        const int slot = idx % kStages;
+                        const uint32_t use = idx / kStages;
+                        if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag,
+                                        a, kErrTimeoutLoad)) {
+                            ok = false;
+                            break;
+                        }
+                        if (a.stall_inject && gstep == 0 && kv == 1) {
+                            // Test hook: never deliver V_0, so the MMA warp's wait
+                            // runs out and the abort path is exercised without
+                            // any fault.
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t bar = smem_u32(&sm.bar_full[slot]);
+                        mbar_arrive_expect_tx(bar, kTileBytes);
+                        tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), kv ? &a.tm_v : &a.tm_k,
+                                               bar, cur.off_k + (cur.j0 + j) * kBlockN, cur.kvh,
+                                               kVarlen ? 0 : cur.b, pol_kv);
+                        issued = idx + 1;
+                    }
+                    // The next tile's Q goes out once this tile's first K/V is
+                    // on its way.
+                    if (ok && j == 0 && have_nxt) ok = issue_q(nxt);
+                }
+                cur = nxt;
+                have_cur = have_nxt;
             }
             if (!ok || *abort_flag) {
                 // Let every copy this warp started land before the CTA exits.
-                for (int i = 0; i < kTilesPerCta; ++i)
-                    if (n_kv(i) > 0) drain_phase(smem_u32(&sm.bar_q[i]), 0, a);
-                for (int idx = max(0, issued - kStages); idx < issued; ++idx) {
-                    if (a.stall_inject && idx == 1) continue;
+                for (int t = max(0, q_issued - 2); t < q_issued; ++t)
+                    drain_phase(smem_u32(&sm.bar_qfull[t & 1]), (t >> 1) & 1, a);
+                for (int idx = max(0, issued - kStages); idx < issued; ++idx)
                     drain_phase(smem_u32(&sm.bar_full[idx % kStages]), (idx / kStages) & 1, a);
-                }
             }
         }
         __syncwarp();
@@ -445,12 +520,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         auto commit = [&](uint64_t* bar) {
             if (leader) mma_commit(smem_u32(bar));
         };
-        // S_i = Q_i K^T : M=128, N=128, K=64 as 4 x K16, 32 bytes (descriptor
-        // +2) apart inside the 128-byte swizzled rows.
-        auto issue_s = [&](int i, int slot) {
-            const uint64_t da = dq0 + (uint64_t)(i * (kTileBytes >> 4));
+        // S = Q K^T : M=128, N=128, K=64 as 4 x K16, 32 bytes (descriptor +2)
+        // apart inside the 128-byte swizzled rows.
+        auto issue_s = [&](int qb, int slot) {
+            const uint64_t da = dq0 + (uint64_t)(qb * (kTileBytes >> 4));
             const uint64_t db = dk0 + (uint64_t)(slot * (kTileBytes >> 4));
-            const uint32_t d = tmem + col_s(i);
+            const uint32_t d = tmem + kColS;
             if (leader) {
                 mma_ss(d, da, db, idesc_qk, 0u);
                 mma_ss(d, da + 2, db + 2, idesc_qk, 1u);
@@ -458,13 +533,13 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 mma_ss(d, da + 6, db + 6, idesc_qk, 1u);
             }
         };
-        // O_i += P_i V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the
-        // TMEM A operand; V is MN-major in shared memory, 16 keys = two 8-row
+        // O += P V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the TMEM A
+        // operand; V is MN-major in shared memory, 16 keys = two 8-row
         // swizzle atoms = 2048 bytes (descriptor +128) per step.
-        auto issue_pv = [&](int i, int slot, bool accumulate) {
+        auto issue_pv = [&](int slot, bool accumulate) {
             const uint64_t db = dv0 + (uint64_t)(slot * (kTileBytes >> 4));
-            const uint32_t d = tmem + col_o(i);
-            const uint32_t pa = tmem + col_p(i);
+            const uint32_t d = tmem + kColO;
+            const uint32_t pa = tmem + kColP;
             if (leader) {
                 mma_ts(d, pa, db, idesc_pv, accumulate ? 1u : 0u);
 #pragma unroll
@@ -472,66 +547,49 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     mma_ts(d, pa + kk * 8, db + (uint64_t)(kk * 128), idesc_pv, 1u);
             }
         };
-
-        for (int i = 0; i < kTilesPerCta && ok; ++i)
-            if (n_kv(i) > 0) ok = wait_all(&sm.bar_q[i], 0);
-        if (ok && n_max > 0) {
-            ok = wait_all(&sm.bar_full[slot_of(0)], full_parity(0));
-            if (ok) {
-                tc_fence_after();
-                for (int i = 0; i < kTilesPerCta; ++i) {
-                    if (n_kv(i) == 0) continue;
-                    issue_s(i, slot_of(0));
-                    commit(&sm.bar_s[i]);
-                }
-                commit(&sm.bar_empty[slot_of(0)]);
-            }
-        }
-        // Steady state, per KV tile j:
-        //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
-        //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
-        for (int j = 0; j < n_max && ok; ++j) {
-            const int v_idx = 2 * j + 1;
-            const int k_idx = 2 * j + 2;
-            bool k_used = false;
-            for (int i = 0; i < kTilesPerCta; ++i) {
-                if (j + 1 >= n_kv(i)) continue;
-                if (!k_used) {
-                    ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
-                    if (!ok) break;
-                    TRACE_EV(2, j, 4);
-                    k_used = true;
-                }
-                ok = wait_all(&sm.bar_sfree[i], j & 1);
-                if (!ok) break;
-                tc_fence_after();
-                TRACE_EV(2, j, i);
-                issue_s(i, slot_of(k_idx));
-                TRACE_EV(3, j, i * 2);
-                commit(&sm.bar_s[i]);
-                TRACE_EV(3, j, i * 2 + 1);
-            }
-            if (!ok) break;
-            if (k_used) commit(&sm.bar_empty[slot_of(k_idx)]);
-            TRACE_EV(2, j, 7);
-            ok = wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx));
-            if (!ok) break;
-            TRACE_EV(2, j, 5);
-            for (int i = 0; i < kTilesPerCta; ++i) {
-                if (j >= n_kv(i)) continue;
-                ok = wait_all(&sm.bar_p[i], j & 1);
-                if (!ok) break;
-                tc_fence_after();
-                TRACE_EV(2, j, 2 + i);
-                issue_pv(i, slot_of(v_idx), j > 0);
-                TRACE_EV(3, j, 4 + i * 2);
-                commit(&sm.bar_pv[i]);
-                if (j == n_kv(i) - 1) commit(&sm.bar_o[i]);
-                TRACE_EV(3, j, 5 + i * 2);
-            }
-            if (!ok) break;
+        // O += P(g) V(g) of flat step g; `first` starts a tile (O overwritten,
+        // after the previous tile's O was read out), tile = its tile count.
+        auto step_pv = [&](int g, bool first, int tile) -> bool {
+            const int v_idx = 2 * g + 1;
+            if (!wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx))) return false;
+            if (!wait_all(&sm.bar_p, g & 1)) return false;
+            if (first && tile > 0 && !wait_all(&sm.bar_ofree, (tile - 1) & 1)) return false;
+            tc_fence_after();
+            issue_pv(slot_of(v_idx), !first);
+            commit(&sm.bar_pv);
             commit(&sm.bar_empty[slot_of(v_idx)]);
+            return true;
+        };
+
+        int k = 0;
+        int g = 0;      // flat KV step counter
+        int tile = 0;   // tiles with work seen by this CTA
+        int pend_g = -1, pend_tile = 0;
+        bool pend_first = false;
+        TileWork w;
+        while (ok && next_tile(k, w)) {
+            const int qb = tile & 1;
+            ok = wait_all(&sm.bar_qfull[qb], (tile >> 1) & 1);
+            for (int j = 0; j < w.n && ok; ++j, ++g) {
+                // S(g) as soon as the softmax has read S(g-1) and K landed ...
+                const int k_idx = 2 * g;
+                ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
+                if (ok && g > 0) ok = wait_all(&sm.bar_sfree, (g - 1) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                issue_s(qb, slot_of(k_idx));
+                commit(&sm.bar_s);
+                commit(&sm.bar_empty[slot_of(k_idx)]);
+                if (j == w.n - 1) commit(&sm.bar_qempty[qb]);
+                // ... then O += P(g-1) V(g-1) once P(g-1) is written.
+                if (pend_g >= 0) ok = step_pv(pend_g, pend_first, pend_tile);
+                pend_g = g;
+                pend_first = (j == 0);
+                pend_tile = tile;
+            }
+            ++tile;
         }
+        if (ok && pend_g >= 0) ok = step_pv(pend_g, pend_first, pend_tile);
         // All MMAs this warp issued must finish before TMEM is freed.
         commit(&sm.bar_drain);
         drain_phase(smem_u32(&sm.bar_drain), 0, a);
@@ -539,232 +597,178 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     }
     } else {
         regs_inc<kRegsSoftmax>();
-        // ------------------------------------------------------ softmax groups
-        const int i = warp >> 2;                    // query tile of this group
-        const int t = threadIdx.x & (kBlockM - 1);  // row inside the tile == TMEM lane
-        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + lane_base + col_s(i);
-        const uint32_t tO = tmem + lane_base + col_o(i);
-        const int n = n_kv(i);
-        const int tile_row0 = w.row0 + i * kBlockM;
-        const int row = tile_row0 + t;
-        const int shift = w.seqlen_k - w.seqlen_q;
+        // ------------------------------------------------------ softmax group
+        const int t = threadIdx.x;  // row inside the tile == TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t tS = tmem + lane_base + kColS;
+        const uint32_t tO = tmem + lane_base + kColO;
+        const uint32_t tP = tmem + lane_base + kColP;
         const float scale = a.scale;
-        // Keys visible to this row: [0, key_lim).
-        const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
-
-        float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
-        float l_run = 0.0f;       // running sum of un-normalised P
         bool ok = true;
+        int g = 0;      // flat KV step counter
+        TileWork w;
+        for (int k = 0; ok; ++k) {
+            const int x = work_index(a, k);
+            if (x == -1) break;
+            if (x < 0 || !decode_work<kCausal, kVarlen>(a, x, w)) continue;
+            const int n = w.n;
+            const int row = w.row0 + t;
+            const int shift = w.seqlen_k - w.seqlen_q;
+            // Keys visible to this row: [0, key_lim).
+            const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
 
-        const uint32_t tP = tmem + lane_base + col_p(i);
-        for (int j = 0; j < n; ++j) {
-            if (t == 0) TRACE_EV(i, j, 0);
-            bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
-            if (t == 0) TRACE_EV(i, j, 1);
-            if (!__all_sync(0xffffffffu, got)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t r[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) reg_fence(r[c]);
-            // S_i now lives in registers: the MMA warp may overwrite it with
-            // S_i(j+1) while this group computes P_i(j).
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sm.bar_sfree[i]));
-            if (t == 0) TRACE_EV(i, j, 2);
+            float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
+            float l_run = 0.0f;       // running sum of un-normalised P
 
-            const int k0 = (w.j0 + j) * kBlockN;
-            const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
-                                   (kCausal && k0 + kBlockN - 1 > tile_row0 + shift);
-            if (need_mask) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
-            }
-            // Row max: 8 independent 3-input-max chains.
-            float mx[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
-#pragma unroll
-                for (int e = 1; e < 15; e += 2)
-                    mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
-                mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
-            }
-            const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
-                                        fmaxf(mx[6], mx[7]));
-            const float m_new = fmaxf(m_run, row_max);
-            const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
-            float alpha = 1.0f;
-            if (upd) {
-                alpha = ex2_approx((m_run - m_new) * scale);
-                m_run = m_new;
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            const float neg_ms = kPLog2Bias - m_use * scale;
-            if (t == 0) TRACE_EV(i, j, 6);
-            const float2 scale2 = make_float2(scale, scale);
-            const float2 neg2 = make_float2(neg_ms, neg_ms);
-            float2 sum[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
-            uint32_t p[2][32];
-            // P = exp2(S*scale - m*scale).  On tiles without masking a fixed
-            // share of the pairs (kExpPolyPairs of every 16) runs the
-            // polynomial exp2 on the FMA/ALU pipes, relieving MUFU; masked
-            // tiles (which may hold -inf) use MUFU ex2 only.
-            auto exp_tile = [&](auto poly_tag) {
-                constexpr bool kPoly = decltype(poly_tag)::value;
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const int pr = e >> 1;  // pair index in the chunk
-                        const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
-                                                           __uint_as_float(r[c][e + 1])),
-                                               scale2, neg2);
-                        float2 pp;
-                        if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
-                            pp = exp2_poly2(x);
-                        else
-                            pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-                        sum[pr & 3] = fadd2(sum[pr & 3], pp);
-                        p[c >> 1][(c & 1) * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
-                    }
-            };
-            if (need_mask) exp_tile(std::false_type{});
-            else exp_tile(std::true_type{});
-            const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
-            l_run = fmaf(l_run, alpha, s01.x + s01.y);
-            if (t == 0) TRACE_EV(i, j, 3);
-
-            if (j > 0) {
-                // P_i(j-1) must be consumed (and O_i settled) before P_i(j) and the
-                // O_i rescale are written.
-                got = wait_phase(smem_u32(&sm.bar_pv[i]), (j - 1) & 1, abort_flag, a,
-                                 kErrTimeoutSoftmax);
+            for (int j = 0; j < n; ++j, ++g) {
+                bool got = wait_phase(smem_u32(&sm.bar_s), g & 1, abort_flag, a,
+                                      kErrTimeoutSoftmax);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-            }
-            if (t == 0) TRACE_EV(i, j, 4);
-            tmem_st32(tP, p[0]);
-            tmem_st32(tP + 32, p[1]);
-            if (j > 0 && __any_sync(0xffffffffu, upd)) {
+                uint32_t r[4][32];
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(tO + c * 32, o);
-                    tmem_wait_ld();
-                    reg_fence(o);
-                    const float2 a2 = make_float2(alpha, alpha);
+                for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        const float2 v2 = fmul2(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
-                        o[e] = __float_as_uint(v2.x);
-                        o[e + 1] = __float_as_uint(v2.y);
-                    }
-                    tmem_st32(tO + c * 32, o);
-                }
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sm.bar_p[i]));
-            if (t == 0) TRACE_EV(i, j, 5);
-        }
+                for (int c = 0; c < 4; ++c) reg_fence(r[c]);
+                // S now lives in registers: the MMA warp may overwrite it with
+                // S(g+1) while this group computes P(g).
+                tc_fence_before();
+                mbar_arrive(smem_u32(&sm.bar_sfree));
 
-        // ---------------------------------------------------- epilogue
-        if (ok && n > 0) {
-            bool got = wait_phase(smem_u32(&sm.bar_o[i]), 0, abort_flag, a, kErrTimeoutSoftmax);
-            ok = __all_sync(0xffffffffu, got);
-        }
-        if (ok) {
+                const int k0 = (w.j0 + j) * kBlockN;
+                const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
+                                       (kCausal && k0 + kBlockN - 1 > w.row0 + shift);
+                if (need_mask) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
+                }
+                // Row max: 8 independent 3-input-max chains.
+                float mx[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
+#pragma unroll
+                    for (int e = 1; e < 15; e += 2)
+                        mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+                    mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
+                }
+                const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]),
+                                            fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+                const float m_new = fmaxf(m_run, row_max);
+                const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
+                float alpha = 1.0f;
+                if (upd) {
+                    alpha = ex2_approx((m_run - m_new) * scale);
+                    m_run = m_new;
+                }
+                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                const float neg_ms = kPLog2Bias - m_use * scale;
+                const float2 scale2 = make_float2(scale, scale);
+                const float2 neg2 = make_float2(neg_ms, neg_ms);
+                float2 sum[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
+                uint32_t p[2][32];
+                // P = exp2(S*scale - m*scale).  On tiles without masking a
+                // fixed share of the pairs (kExpPolyPairs of every 16) runs the
+                // polynomial exp2 on the FMA/ALU pipes, relieving MUFU; masked
+                // tiles (which may hold -inf) use MUFU ex2 only.
+                auto exp_tile = [&](auto poly_tag) {
+                    constexpr bool kPoly = decltype(poly_tag)::value;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const int pr = e >> 1;  // pair index in the chunk
+                            const float2 xx = ffma2(make_float2(__uint_as_float(r[c][e]),
+                                                                __uint_as_float(r[c][e + 1])),
+                                                    scale2, neg2);
+                            float2 pp;
+                            if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
+                                pp = exp2_poly2(xx);
+                            else
+                                pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+                            sum[pr & 3] = fadd2(sum[pr & 3], pp);
+                            p[c >> 1][(c & 1) * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
+                        }
+                };
+                if (need_mask) exp_tile(std::false_type{});
+                else exp_tile(std::true_type{});
+                const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
+                l_run = fmaf(l_run, alpha, s01.x + s01.y);
+
+                if (g > 0) {
+                    // P(g-1) must be consumed (and O settled) before P(g) and
+                    // the O rescale are written.
+                    got = wait_phase(smem_u32(&sm.bar_pv), (g - 1) & 1, abort_flag, a,
+                                     kErrTimeoutSoftmax);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+                tmem_st32(tP, p[0]);
+                tmem_st32(tP + 32, p[1]);
+                if (j > 0 && __any_sync(0xffffffffu, upd)) {
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
+                        reg_fence(o);
+                        const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2) {
+                            const float2 v2 = fmul2(
+                                make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
+                            o[e] = __float_as_uint(v2.x);
+                            o[e + 1] = __float_as_uint(v2.y);
+                        }
+                        tmem_st32(tO + c * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(smem_u32(&sm.bar_p));
+            }
+            if (!ok) break;
+
+            // ---------------------------------------------------- epilogue
             uint32_t o[2][32];
-            if (n > 0) {
+            if (n == 0) {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) o[0][c] = o[1][c] = 0u;
+            } else {
+                // The tile's last P V is done: read O out, then hand the
+                // accumulator to the next tile's first P V.
+                bool got = wait_phase(smem_u32(&sm.bar_pv), (g - 1) & 1, abort_flag, a,
+                                      kErrTimeoutSoftmax);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 tmem_ld32(tO, o[0]);
                 tmem_ld32(tO + 32, o[1]);
                 tmem_wait_ld();
                 reg_fence(o[0]);
                 reg_fence(o[1]);
+                tc_fence_before();
+                mbar_arrive(smem_u32(&sm.bar_ofree));
             }
-            if (w.partial) {
-                // Split-KV: this item's normalised partial O (fp32) and LSE;
-                // the combine kernel merges the splits of each query block.
-                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-                const size_t prow = (size_t)blockIdx.x * kRowsPerCta + (size_t)i * kBlockM + t;
-                float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim);
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    float v[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int col = c * 4 + e;
-                        v[e] = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
-                    }
-                    dst[c] = make_float4(v[0], v[1], v[2], v[3]);
-                }
-                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-                a.part_lse[prow] = (l_run > 0.0f)
-                                       ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
-                                             0.69314718055994531f
-                                       : -INFINITY;
-            } else if (row < w.seqlen_q) {
-                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-                uint16_t* orow;
-                if constexpr (kVarlen) {
-                    orow = a.o + (long long)w.h * a.nhead_stride_o +
-                           (long long)(w.off_q + row) * a.stride_o;
-                } else {
-                    orow = a.o + (long long)w.b * a.batch_stride_o +
-                           (long long)w.h * a.nhead_stride_o + (long long)row * a.stride_o;
-                }
-                uint4* dst = reinterpret_cast<uint4*>(orow);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int col = c * 8 + e * 2;
-                        const float v0 = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
-                        const float v1 = n > 0 ? __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l : 0.0f;
-#ifdef FMHA_O_ROUND_TRUNC
-                        pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
-#else
-                        pk[e] = pack_bf16_rne(v0, v1);
-#endif
-                    }
-                    dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                }
-                if (a.lse != nullptr) {
-                    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-                    const float lse = (l_run > 0.0f)
-                                          ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
-                                                0.69314718055994531f
-                                          : -INFINITY;
-                    long long idx;
-                    if constexpr (kVarlen) {
-                        idx = (long long)w.h * a.total_q + w.off_q + row;
-                    } else {
-                        idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
-                    }
-                    a.lse[idx] = lse;
-                }
-            }
+            store_row<kVarlen>(a, w, t, o, n > 0, m_run, l_run);
         }
-}
+    }
 
     // ---------------------------------------------------------- teardown
     tc_fence_before();
@@ -775,7 +779,6 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     }
 }
 
-
 // Split-KV merge of one query row: partial slots [slot0, slot0 + nparts) of
 // query block mblk of (batch, head) hb; LSE = log(sum_s exp(lse_s)),
 // O = sum_s exp(lse_s - LSE) * O_s, rounded to bf16 like the main epilogue;
@@ -784,24 +787,27 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 template <bool kVarlen>
 __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk, int slot0,
                                           int nparts, int r) {
+    // Malformed list entries are skipped before any address is formed.
+    if (hb < 0 || hb >= a.num_hb || mblk < 0 || mblk >= a.m_blocks) return;
     const int h = hb % a.nhead_q, b = hb / a.nhead_q;
     int seqlen_q = a.seqlen_q, off_q = 0;
     if constexpr (kVarlen) {
         off_q = a.seqstart_q[b];
         seqlen_q = a.seqstart_q[b + 1] - off_q;
+        if (off_q < 0 || seqlen_q < 0 || off_q + seqlen_q > a.total_q) return;
     }
-    const int row = mblk * kRowsPerCta + r;
+    const int row = mblk * kBlockM + r;
     if (row >= seqlen_q) return;
     float mx = -INFINITY;
     for (int s = 0; s < nparts; ++s)
-        mx = fmaxf(mx, a.part_lse[(size_t)(slot0 + s) * kRowsPerCta + r]);
+        mx = fmaxf(mx, a.part_lse[(size_t)(slot0 + s) * kBlockM + r]);
     float acc[kHeadDim];
 #pragma unroll
     for (int d = 0; d < kHeadDim; ++d) acc[d] = 0.0f;
     float wsum = 0.0f;
     if (mx != -INFINITY) {
         for (int s = 0; s < nparts; ++s) {
-            const size_t prow = (size_t)(slot0 + s) * kRowsPerCta + r;
+            const size_t prow = (size_t)(slot0 + s) * kBlockM + r;
             const float l = a.part_lse[prow];
             if (l == -INFINITY) continue;
             const float wgt = __expf(l - mx);
@@ -851,12 +857,10 @@ __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk,
 template <bool kVarlen>
 __global__ void __launch_bounds__(128)
 fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
-    constexpr int kParts = kRowsPerCta / 128;       // 128-row CTAs per query block
-    const int item_block = blockIdx.x / kParts;
-    const int r = (blockIdx.x % kParts) * 128 + threadIdx.x;
+    const int item_block = blockIdx.x;
     if (item_block >= nblocks) return;
     merge_row<kVarlen>(a, a.tiles[2 * item_block], a.tiles[2 * item_block + 1],
-                       item_block * a.num_splits, a.num_splits, r);
+                       item_block * a.num_splits, a.num_splits, threadIdx.x);
 }
 
 // Work-item combine: block x merges the run of consecutive partial items of
@@ -869,11 +873,14 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
     __shared__ int run_end;
     const int x = blockIdx.x;
     const int4* items = reinterpret_cast<const int4*>(a.items);
+    // A partial item has a well-formed KV range; malformed items were skipped
+    // by the main kernel (no partial result) and take no part in any run.
+    auto partial = [](const int4& e) { return e.w >= 0 && e.z >= 0 && e.z <= e.w; };
     const int4 it = items[x];
-    if (it.w < 0) return;  // direct item: O already written
+    if (!partial(it)) return;  // direct (O already written) or malformed item
     if (x > 0) {
         const int4 prev = items[x - 1];
-        if (prev.w >= 0 && prev.x == it.x && prev.y == it.y) return;  // not the run's head
+        if (partial(prev) && prev.x == it.x && prev.y == it.y) return;  // not the run's head
     }
     int n = 0;
     for (int base = x + 1;; base += 128) {
@@ -882,7 +889,7 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
         const int y = base + (int)threadIdx.x;
         if (y < n_items) {
             const int4 nx = items[y];
-            if (nx.w < 0 || nx.x != it.x || nx.y != it.y) atomicMin(&run_end, y);
+            if (!partial(nx) || nx.x != it.x || nx.y != it.y) atomicMin(&run_end, y);
         }
         __syncthreads();
         const int e = run_end;
@@ -899,6 +906,7 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
 
 struct DeviceContext {
     bool ready = false;
+    int num_sms = 0;
     int* err_word = nullptr;
 };
 
@@ -907,56 +915,52 @@ std::vector<DeviceContext> g_devices;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 unsigned long long g_wait_limit_ns = 2000000000ull;
 int g_stall_inject = 0;
-unsigned long long* g_trace = nullptr;
+int g_max_ctas = 0;  // 0: kCtasPerSm per SM (persistent); < 0: one CTA per item
 
-template <bool C, bool V>
-constexpr size_t kernel_smem_bytes() {
-    return sizeof(SharedStorage) + 1024;
+constexpr size_t kSmemBytes = sizeof(SharedStorage) + 1024;
+
+// Per-process, once: the driver's tensor-map encoder.  Caller holds g_mutex.
+int ensure_encoder() {
+    if (g_encode != nullptr) return FMHA_OK;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        fn == nullptr)
+        return FMHA_ERR_DEVICE;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return FMHA_OK;
 }
 
-// Largest shared-memory carveout, so kCtasPerSm CTAs fit on one SM.
-void set_carveout() {
-    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
-                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
-                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
-                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
-                         cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+// Per device, once (device current): check it is an sm_100 part, read its SM
+// count and set the kernels' shared-memory attributes.  Allocates nothing.
+int prepare_device(int dev, int* num_sms) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
+    *num_sms = prop.multiProcessorCount;
+    const int smem = (int)kSmemBytes;
+    auto set = [smem](const void* fn) {
+        cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    };
+    set(reinterpret_cast<const void*>(fmha_fwd_d64_sm100_kernel<false, false>));
+    set(reinterpret_cast<const void*>(fmha_fwd_d64_sm100_kernel<true, false>));
+    set(reinterpret_cast<const void*>(fmha_fwd_d64_sm100_kernel<false, true>));
+    set(reinterpret_cast<const void*>(fmha_fwd_d64_sm100_kernel<true, true>));
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
 }
 
 int ensure_context(int dev, DeviceContext** out) {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (g_encode == nullptr) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            fn == nullptr) {
-            return FMHA_ERR_DEVICE;
-        }
-        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+    int st = ensure_encoder();
+    if (st != FMHA_OK) return st;
     if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1);
     DeviceContext& ctx = g_devices[dev];
     if (!ctx.ready) {
-        cudaDeviceProp prop;
-        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
-        if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
+        if ((st = prepare_device(dev, &ctx.num_sms)) != FMHA_OK) return st;
         if (cudaMalloc(&ctx.err_word, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
         if (cudaMemset(ctx.err_word, 0, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
-        const int smem = (int)kernel_smem_bytes<false, false>();
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        set_carveout();
-        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         ctx.ready = true;
     }
     *out = &ctx;
@@ -990,10 +994,12 @@ bool stride_ok(long long s, int extent) {
     return s > 0 && (s % 8) == 0 && s * 2 < (1ll << 40);
 }
 
-int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
-           cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1,
-           int num_splits = 1, float* workspace = nullptr, const int32_t* items = nullptr,
-           int n_items = 0) {
+// Checks the problem description and fills everything of the kernel
+// arguments except the work description, error word and launch options.
+// Sets *empty when there is nothing to compute.
+int prepare_args(const FmhaFwdParams* p, int batch, bool varlen, int total_q, int total_k,
+                 KernelArgs& a, bool* empty) {
+    *empty = false;
     if (p == nullptr || batch <= 0) return FMHA_ERR_ARG;
     if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
     if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
@@ -1015,15 +1021,18 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     if ((p->stride_o % 8) != 0 || (p->nhead_stride_o % 8) != 0 ||
         (!varlen && (p->batch_stride_o % 8) != 0))
         return FMHA_ERR_ARG;
-    if (p->seqlen_q == 0 || rows_q == 0) return FMHA_OK;  // nothing to compute
+    if (p->seqlen_q == 0 || rows_q == 0) {
+        *empty = true;
+        return FMHA_OK;
+    }
+    const int m_blocks = (p->seqlen_q + kBlockM - 1) / kBlockM;
+    if ((long long)m_blocks * p->nhead_q * batch > 0x7fffffffll) return FMHA_ERR_ARG;
 
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
-    DeviceContext* ctx = nullptr;
-    int st = ensure_context(dev, &ctx);
-    if (st != FMHA_OK) return st;
-
-    KernelArgs a;
+    int st;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        if ((st = ensure_encoder()) != FMHA_OK) return st;
+    }
     memset(&a, 0, sizeof(a));
     const int rank = varlen ? 3 : 4;
     const int mb = varlen ? 1 : batch;
@@ -1040,8 +1049,8 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
         return st;
     a.o = p->o;
     a.lse = p->lse;
-    a.seqstart_q = p->seqstart_q;
-    a.seqstart_k = p->seqstart_k;
+    a.seqstart_q = varlen ? p->seqstart_q : nullptr;
+    a.seqstart_k = varlen ? p->seqstart_k : nullptr;
     a.stride_o = p->stride_o;
     a.nhead_stride_o = p->nhead_stride_o;
     a.batch_stride_o = p->batch_stride_o;
@@ -1051,60 +1060,85 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     a.nhead_k = p->nhead_k;
     a.total_q = total_q;
     a.scale = p->scale;
-    a.err_word = ctx->err_word;
     a.wait_limit_ns = g_wait_limit_ns;
-    a.stall_inject = g_stall_inject;
-    a.trace = g_trace;
-
-    const int m_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
-    const long long nblocks = (long long)m_blocks * p->nhead_q * batch;
-    if (nblocks > 0x7fffffffll) return FMHA_ERR_ARG;
     a.m_blocks = m_blocks;
     a.num_hb = p->nhead_q * batch;
+    a.num_splits = 1;
     {
         // Group (batch, head) pairs so a group's K/V (read by all its blocks)
         // fits in ~48 MB of the 126 MB L2.
-        const long long kv_bytes = (long long)(varlen ? p->seqlen_k : rows_k) * kHeadDim * 2 * 2;
+        const long long kv_bytes = (long long)p->seqlen_k * kHeadDim * 2 * 2;
         const long long g = kv_bytes > 0 ? (48ll << 20) / kv_bytes : a.num_hb;
         a.head_group = (int)std::max(1ll, std::min<long long>(g, a.num_hb));
     }
-    dim3 grid((unsigned)nblocks, 1, 1);
+    return FMHA_OK;
+}
+
+// Persistent grid: at most kCtasPerSm CTAs per SM (or the caller's limit),
+// never more CTAs than work items.
+unsigned grid_for(int n_work, int num_sms) {
+    long long cap = (long long)kCtasPerSm * num_sms;
+    if (g_max_ctas > 0) cap = std::min<long long>(cap, g_max_ctas);
+    if (g_max_ctas < 0) cap = n_work;
+    return (unsigned)std::max(1ll, std::min<long long>(cap, n_work));
+}
+
+int launch_main(const KernelArgs& a, bool causal, bool varlen, unsigned grid,
+                cudaStream_t stream) {
+    const dim3 block(kThreads);
+    if (causal) {
+        if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, kSmemBytes, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<true, false><<<grid, block, kSmemBytes, stream>>>(a);
+    } else {
+        if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, kSmemBytes, stream>>>(a);
+        else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, kSmemBytes, stream>>>(a);
+    }
+    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
+}
+
+int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int total_q, int total_k,
+           cudaStream_t stream, const int32_t* tiles = nullptr, int ntiles = -1,
+           int num_splits = 1, float* workspace = nullptr, const int32_t* items = nullptr,
+           int n_items = 0) {
+    KernelArgs a;
+    bool empty = false;
+    int st = prepare_args(p, batch, varlen, total_q, total_k, a, &empty);
+    if (st != FMHA_OK || empty) return st;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
+    DeviceContext* ctx = nullptr;
+    if ((st = ensure_context(dev, &ctx)) != FMHA_OK) return st;
+    a.err_word = ctx->err_word;
+    a.stall_inject = g_stall_inject;
+
+    a.n_work = a.m_blocks * a.num_hb;
     a.tiles = tiles;
-    a.num_splits = 1;
     if (tiles != nullptr) {
         if (ntiles == 0) return FMHA_OK;
-        grid = dim3((unsigned)ntiles, 1, 1);
+        a.n_work = ntiles;
         if (num_splits > 1) {
             a.num_splits = num_splits;
             a.part_o = workspace;
-            a.part_lse = workspace + (size_t)ntiles * num_splits * kRowsPerCta * kHeadDim;
-            grid = dim3((unsigned)(ntiles * num_splits), 1, 1);
+            a.part_lse = workspace + (size_t)ntiles * num_splits * kBlockM * kHeadDim;
+            a.n_work = ntiles * num_splits;
         }
     }
     if (items != nullptr) {
         if (n_items == 0) return FMHA_OK;
         a.items = items;
         a.part_o = workspace;
-        a.part_lse = workspace + (size_t)n_items * kRowsPerCta * kHeadDim;
-        grid = dim3((unsigned)n_items, 1, 1);
+        a.part_lse = workspace + (size_t)n_items * kBlockM * kHeadDim;
+        a.n_work = n_items;
     }
-    dim3 block(kThreads);
-    const size_t smem = kernel_smem_bytes<false, false>();
-    if (causal) {
-        if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, smem, stream>>>(a);
-        else fmha_fwd_d64_sm100_kernel<true, false><<<grid, block, smem, stream>>>(a);
-    } else {
-        if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
-        else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
-    }
+    if ((st = launch_main(a, causal, varlen, grid_for(a.n_work, ctx->num_sms), stream)) !=
+        FMHA_OK)
+        return st;
     if (items != nullptr) {
-        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         dim3 cgrid((unsigned)n_items, 1, 1);
         if (varlen) fmha_fwd_d64_items_combine<true><<<cgrid, 128, 0, stream>>>(a, n_items);
         else fmha_fwd_d64_items_combine<false><<<cgrid, 128, 0, stream>>>(a, n_items);
     } else if (a.num_splits > 1) {
-        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
-        dim3 cgrid((unsigned)(ntiles * (kRowsPerCta / 128)), 1, 1);
+        dim3 cgrid((unsigned)ntiles, 1, 1);
         if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, 128, 0, stream>>>(a, ntiles);
         else fmha_fwd_d64_splitkv_combine<false><<<cgrid, 128, 0, stream>>>(a, ntiles);
     }
@@ -1131,6 +1165,7 @@ static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocHeaderInts + 
 
 struct NoAllocDevice {
     bool ready = false;
+    int num_sms = 0;
     int32_t* scratch = nullptr;  // device address of g_noalloc_scratch on that device
 };
 std::vector<NoAllocDevice> g_noalloc;
@@ -1138,41 +1173,21 @@ std::vector<NoAllocDevice> g_noalloc;
 // Once per device, with that device current: resolve the device address of
 // the scratch array (the host-side name is only a stand-in) and set the
 // kernels' shared-memory attribute.  Allocates nothing.
-int noalloc_setup(int dev, int32_t** scratch) {
+int noalloc_setup(int dev, NoAllocDevice** out) {
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (g_encode == nullptr) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
-                cudaSuccess ||
-            fn == nullptr)
-            return FMHA_ERR_DEVICE;
-        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
+    int st = ensure_encoder();
+    if (st != FMHA_OK) return st;
     if ((int)g_noalloc.size() <= dev) g_noalloc.resize(dev + 1);
     NoAllocDevice& d = g_noalloc[dev];
     if (!d.ready) {
-        cudaDeviceProp prop;
-        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
-        if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
+        if ((st = prepare_device(dev, &d.num_sms)) != FMHA_OK) return st;
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
             return FMHA_ERR_LAUNCH;
-        const int smem = (int)kernel_smem_bytes<false, false>();
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<false, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        cudaFuncSetAttribute(fmha_fwd_d64_sm100_kernel<true, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        set_carveout();
-        if (cudaGetLastError() != cudaSuccess) return FMHA_ERR_LAUNCH;
         d.scratch = static_cast<int32_t*>(ptr);
         d.ready = true;
     }
-    *scratch = d.scratch;
+    *out = &d;
     return FMHA_OK;
 }
 
@@ -1182,64 +1197,30 @@ int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, 
     if (ntiles > kNoAllocMaxTiles) return FMHA_ERR_SCRATCH;
     if (ntiles > 0 && host_tiles == nullptr) return FMHA_ERR_ARG;
     const bool varlen = p->seqstart_q != nullptr;
-    if (!p->q || !p->k || !p->v || !p->o) return FMHA_ERR_ARG;
-    if (p->nhead_q <= 0 || p->nhead_k <= 0 || p->nhead_q % p->nhead_k != 0) return FMHA_ERR_ARG;
-    if (p->seqlen_q < 0 || p->seqlen_k < 0) return FMHA_ERR_ARG;
-    if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
-        return FMHA_ERR_ARG;
-    if (varlen && (!p->seqstart_k || total_q < 0 || total_k < 0)) return FMHA_ERR_ARG;
-    const int rows_q = varlen ? total_q : p->seqlen_q;
-    const int rows_k = varlen ? total_k : p->seqlen_k;
-    if (!stride_ok(p->stride_q, rows_q) || !stride_ok(p->stride_k, rows_k) ||
-        !stride_ok(p->stride_v, rows_k) || !stride_ok(p->nhead_stride_q, p->nhead_q) ||
-        !stride_ok(p->nhead_stride_k, p->nhead_k) || !stride_ok(p->nhead_stride_v, p->nhead_k))
-        return FMHA_ERR_ARG;
-    if (!varlen && (!stride_ok(p->batch_stride_q, batch) || !stride_ok(p->batch_stride_k, batch) ||
-                    !stride_ok(p->batch_stride_v, batch)))
-        return FMHA_ERR_ARG;
-    if ((p->stride_o % 8) != 0 || (p->nhead_stride_o % 8) != 0 ||
-        (!varlen && (p->batch_stride_o % 8) != 0))
-        return FMHA_ERR_ARG;
-    if (ntiles == 0 || p->seqlen_q == 0 || rows_q == 0) return FMHA_OK;
+    KernelArgs a;
+    bool empty = false;
+    int st = prepare_args(p, batch, varlen, total_q, total_k, a, &empty);
+    if (st != FMHA_OK) return st;
+    // The list is on the host, so every entry is checked before anything is
+    // queued: a (batch, head) index or query block outside the problem is an
+    // argument error, not a silent skip.
+    const long long num_hb = (long long)p->nhead_q * batch;
+    const int m_blocks = (p->seqlen_q + kBlockM - 1) / kBlockM;
+    for (int i = 0; i < ntiles; ++i) {
+        const int32_t hb = host_tiles[2 * i], m = host_tiles[2 * i + 1];
+        if (hb < 0 || hb >= num_hb || m < 0 || m >= m_blocks) return FMHA_ERR_ARG;
+    }
+    if (ntiles == 0 || empty) return FMHA_OK;
 
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
-    int32_t* scratch = nullptr;
-    int st = noalloc_setup(dev, &scratch);
-    if (st != FMHA_OK) return st;
-
-    KernelArgs a;
-    memset(&a, 0, sizeof(a));
-    const int rank = varlen ? 3 : 4;
-    const int mb = varlen ? 1 : batch;
-    const int rk = rows_k > 0 ? rows_k : 1;
-    if ((st = make_map(&a.tm_q, p->q, rank, rows_q, p->nhead_q, mb, p->stride_q,
-                       p->nhead_stride_q, p->batch_stride_q)) != FMHA_OK)
-        return st;
-    if ((st = make_map(&a.tm_k, p->k, rank, rk, p->nhead_k, mb, p->stride_k, p->nhead_stride_k,
-                       p->batch_stride_k)) != FMHA_OK)
-        return st;
-    if ((st = make_map(&a.tm_v, p->v, rank, rk, p->nhead_k, mb, p->stride_v, p->nhead_stride_v,
-                       p->batch_stride_v)) != FMHA_OK)
-        return st;
-    a.o = p->o;
-    a.lse = p->lse;
-    a.seqstart_q = p->seqstart_q;
-    a.seqstart_k = p->seqstart_k;
-    a.stride_o = p->stride_o;
-    a.nhead_stride_o = p->nhead_stride_o;
-    a.batch_stride_o = p->batch_stride_o;
-    a.seqlen_q = p->seqlen_q;
-    a.seqlen_k = p->seqlen_k;
-    a.nhead_q = p->nhead_q;
-    a.nhead_k = p->nhead_k;
-    a.total_q = total_q;
-    a.scale = p->scale;
+    NoAllocDevice* d = nullptr;
+    if ((st = noalloc_setup(dev, &d)) != FMHA_OK) return st;
+    int32_t* scratch = d->scratch;
     a.err_word = scratch;  // header word 0
-    a.wait_limit_ns = g_wait_limit_ns;
     a.stall_inject = 0;
-    a.trace = nullptr;
     a.tiles = scratch + kNoAllocHeaderInts;
+    a.n_work = ntiles;
 
     // The array keeps the previous call's contents: clear the error word and
     // stage this call's work list, in stream order before the kernel.
@@ -1248,19 +1229,12 @@ int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, 
                         sizeof(int32_t) * 2 * (size_t)ntiles, cudaMemcpyHostToDevice,
                         stream) != cudaSuccess)
         return FMHA_ERR_LAUNCH;
-    dim3 grid((unsigned)ntiles, 1, 1);
-    dim3 block(kThreads);
-    const size_t smem = kernel_smem_bytes<false, false>();
-    if (causal) {
-        if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, smem, stream>>>(a);
-        else fmha_fwd_d64_sm100_kernel<true, false><<<grid, block, smem, stream>>>(a);
-    } else {
-        if (varlen) fmha_fwd_d64_sm100_kernel<false, true><<<grid, block, smem, stream>>>(a);
-        else fmha_fwd_d64_sm100_kernel<false, false><<<grid, block, smem, stream>>>(a);
-    }
-    return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
+    return launch_main(a, causal, varlen, grid_for(ntiles, d->num_sms), stream);
 }
 
+// Reads the error word of the allocation-free scratch and clears it, so a
+// second status call (or one after a later failed launch) does not report a
+// stale timeout.
 int noalloc_status(cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return FMHA_ERR_DEVICE;
@@ -1274,7 +1248,13 @@ int noalloc_status(cudaStream_t stream) {
     int h = 0;
     if (cudaMemcpy(&h, scratch, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
         return FMHA_ERR_LAUNCH;
-    return h != 0 ? FMHA_ERR_TIMEOUT : FMHA_OK;
+    if (h != 0) {
+        if (cudaMemsetAsync(scratch, 0, sizeof(int32_t), stream) != cudaSuccess ||
+            cudaStreamSynchronize(stream) != cudaSuccess)
+            return FMHA_ERR_LAUNCH;
+        return FMHA_ERR_TIMEOUT;
+    }
+    return FMHA_OK;
 }
 
 }  // namespace
@@ -1314,11 +1294,11 @@ int fmha_fwd_d64_bf16_tiles(const FmhaFwdParams* params, int batch, int causal, 
     return launch(params, batch, causal != 0, varlen, total_q, total_k, stream, tiles, ntiles);
 }
 
-int fmha_fwd_d64_rows_per_block(void) { return kRowsPerCta; }
+int fmha_fwd_d64_rows_per_block(void) { return kBlockM; }
 
 size_t fmha_fwd_d64_splitkv_workspace_bytes(int ntiles, int num_splits) {
     if (ntiles <= 0 || num_splits <= 0) return 0;
-    return (size_t)ntiles * num_splits * kRowsPerCta * (kHeadDim + 1) * sizeof(float);
+    return (size_t)ntiles * num_splits * kBlockM * (kHeadDim + 1) * sizeof(float);
 }
 
 int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int causal,
@@ -1341,7 +1321,7 @@ int fmha_fwd_d64_bf16_tiles_splitkv(const FmhaFwdParams* params, int batch, int 
 
 size_t fmha_fwd_d64_items_workspace_bytes(int n_items) {
     if (n_items <= 0) return 0;
-    return (size_t)n_items * kRowsPerCta * (kHeadDim + 1) * sizeof(float);
+    return (size_t)n_items * kBlockM * (kHeadDim + 1) * sizeof(float);
 }
 
 int fmha_fwd_d64_bf16_items(const FmhaFwdParams* params, int batch, int causal, int total_q,
@@ -1377,6 +1357,11 @@ int fmha_fwd_d64_status(CUstream_st* stream) {
     return FMHA_OK;
 }
 
+void fmha_fwd_d64_set_max_ctas(int max_ctas) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_max_ctas = max_ctas > 0 ? max_ctas : (max_ctas < 0 ? -1 : 0);
+}
+
 void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns) {
     std::lock_guard<std::mutex> lock(g_mutex);
     g_wait_limit_ns = limit_ns ? limit_ns : 2000000000ull;
@@ -1388,13 +1373,6 @@ void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns) {
 void fmha_fwd_d64_debug_set_stall(int enable) {
     std::lock_guard<std::mutex> lock(g_mutex);
     g_stall_inject = enable;
-}
-
-// Diagnostic hook: device buffer (>= 3*64*8 u64) receiving pipeline event
-// timestamps in builds compiled with -DFMHA_TRACE; NULL disables.
-void fmha_fwd_d64_debug_set_trace(void* device_buffer) {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    g_trace = static_cast<unsigned long long*>(device_buffer);
 }
 
 void fmha_fwd_d64_release(void) {

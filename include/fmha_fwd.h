@@ -178,21 +178,30 @@ int fmha_fwd_d64_bf16_items(const FmhaFwdParams* params, int batch, int causal,
  * keeps its scratch -- the error word and a copy of the work list -- in a
  * fixed 128 KB array inside the library (held by every GPU that loads it).
  *   host_tiles : HOST array of ntiles int32 pairs (b*nhead_q + h, m), as for
- *                fmha_fwd_d64_bf16_tiles; copied in stream order, so it may
- *                be reused once the call returns.
+ *                fmha_fwd_d64_bf16_tiles.  Every entry is checked on the host
+ *                first (FMHA_ERR_ARG, nothing queued, if one names a (batch,
+ *                head) or query block outside the problem).  The list is then
+ *                copied with cudaMemcpyAsync on `stream`.  From pageable
+ *                memory the copy is staged before the call returns, so the
+ *                array may be reused at once; from pinned (page-locked)
+ *                memory the GPU reads it later, in stream order, so it must
+ *                stay unchanged until the stream has passed the call -- and,
+ *                if the call is captured into a CUDA graph, for as long as
+ *                the graph is replayed (each replay reads it again).
  *   ntiles     : at most 16384, else FMHA_ERR_SCRATCH and nothing is launched.
  * The first call on a device resolves the scratch address for that device
  * (make it before any stream capture begins).  All calls share the one array
  * and each call overwrites it: calls whose executions overlap on the GPU race
  * and must be serialised (e.g. one stream).  Read device timeouts with
- * fmha_fwd_d64_noalloc_status. */
+ * fmha_fwd_d64_noalloc_status, which clears the error word it reports. */
 int fmha_fwd_d64_bf16_tiles_noalloc(const FmhaFwdParams* params, int batch, int causal,
                                     int total_q, int total_k, const int32_t* host_tiles,
                                     int ntiles, struct CUstream_st* stream);
 
-/* Synchronizes `stream` and reports FMHA_ERR_TIMEOUT if the last
- * allocation-free call's pipeline waits expired (FMHA_OK otherwise).  No
- * counterpart in the reference. */
+/* Synchronizes `stream` and reports FMHA_ERR_TIMEOUT if a pipeline wait of an
+ * allocation-free call since the last report expired (FMHA_OK otherwise);
+ * the error word is cleared when it is reported.  No counterpart in the
+ * reference. */
 int fmha_fwd_d64_noalloc_status(struct CUstream_st* stream);
 
 /* Synchronizes `stream`, then reads and clears the device error word written
@@ -206,6 +215,14 @@ int fmha_fwd_d64_status(struct CUstream_st* stream);
  * No reference counterpart. */
 void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns);
 
+/* Caps the number of persistent CTAs of subsequent launches on all devices
+ * (each CTA loops over its share of the query tiles); 0 restores the default
+ * of two CTAs per SM; a negative value launches one CTA per work item (no
+ * persistence).  A cap leaves SMs free for work on other streams; every
+ * setting computes the same results.  No reference counterpart (the reference
+ * launches one work group per query tile, src/fused/kernel.cpp:55-99). */
+void fmha_fwd_d64_set_max_ctas(int max_ctas);
+
 /* Releases the per-device launcher context (error word).  No reference
  * counterpart. */
 void fmha_fwd_d64_release(void);
@@ -214,12 +231,12 @@ void fmha_fwd_d64_release(void);
 const char* fmha_fwd_d64_error_string(int status);
 
 /* Query rows per work-list entry of the built kernel (128: one 128-row query
- * tile per CTA, two CTAs per SM).  No reference counterpart. */
+ * tile per work item).  No reference counterpart. */
 int fmha_fwd_d64_rows_per_block(void);
 
 /* Tile geometry of the B200 kernel (informational; callers need not compute
- * launch geometry).  128 query rows per tile, one tile per CTA, 128 keys per
- * KV tile. */
+ * launch geometry).  128 query rows per tile (persistent CTAs, two per SM,
+ * loop over the tiles), 128 keys per KV tile. */
 #define FMHA_B200_BLOCK_M 128
 #define FMHA_B200_ROWS_PER_BLOCK 128 /* query rows per work-list entry (see fmha_fwd_d64_rows_per_block) */
 #define FMHA_B200_BLOCK_N 128

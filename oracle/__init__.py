@@ -280,3 +280,100 @@ def compare(o_kern: np.ndarray, o_ref: np.ndarray, lse_kern=None, lse_ref=None) 
         out["lse_mismatch"] = int((d > LSE_TOL_ABS).sum())
         out["lse_pass"] = out["lse_mismatch"] == 0
     return out
+
+
+# ----------------------------------------------------------------- device oracle
+
+GPU_REF_LIB = os.path.join(ORACLE_DIR, "libgpu_ref.so")
+_glib = None
+
+
+def gpu_ref_lib() -> ctypes.CDLL:
+    global _glib
+    if _glib is None:
+        if not os.path.exists(GPU_REF_LIB):
+            raise FileNotFoundError(f"{GPU_REF_LIB} not built (python oracle/build.py)")
+        _glib = ctypes.CDLL(GPU_REF_LIB)
+        L, I, P = ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p
+        _glib.gpu_ref_fmha_fwd.argtypes = [P, P, P, P, P, ctypes.POINTER(L), I, I, I, I, I, I,
+                                           P, P, I, ctypes.c_float, P]
+        _glib.gpu_ref_fmha_fwd.restype = I
+    return _glib
+
+
+def gpu_ref_fwd(q, k, v, *, layout: str, causal: bool, seqstart_q=None, seqstart_k=None,
+                with_lse: bool = True, stream: int = 0):
+    """Device oracle (gpu_ref.cu, restating gpu_ref.cpp:12-126) on torch CUDA
+    bf16 tensors.  Layouts as fmha_native_b200.params_from_tensors: "bshd",
+    "bhsd" (dense), "thd", "htd" (varlen, int32 seqstart on the device).
+    Returns (O fp32 with q's shape, LSE fp32 [B,H,Sq] / [H,total] or None)."""
+    import torch
+
+    lib = gpu_ref_lib()
+    o = torch.zeros(q.shape, device=q.device, dtype=torch.float32)
+    if layout in ("bshd", "bhsd"):
+        s_ax, h_ax = (1, 2) if layout == "bshd" else (2, 1)
+        batch, sq, sk = q.shape[0], q.shape[s_ax], k.shape[s_ax]
+        hq, hk = q.shape[h_ax], k.shape[h_ax]
+        strides = []
+        for t in (q, k, v, o):
+            st = t.stride()
+            strides += [st[s_ax], st[h_ax], st[0]]
+        lse = torch.full((batch, hq, sq), float("nan"), device=q.device,
+                         dtype=torch.float32) if with_lse else None
+        total_q = 0
+        ssq = ssk = None
+    else:
+        t_ax, h_ax = (0, 1) if layout == "thd" else (1, 0)
+        batch = seqstart_q.numel() - 1
+        hq, hk = q.shape[h_ax], k.shape[h_ax]
+        total_q = q.shape[t_ax]
+        lens_q = (seqstart_q[1:] - seqstart_q[:-1]).max().item() if batch > 0 else 0
+        lens_k = (seqstart_k[1:] - seqstart_k[:-1]).max().item() if batch > 0 else 0
+        sq, sk = int(lens_q), int(lens_k)
+        strides = []
+        for t in (q, k, v, o):
+            st = t.stride()
+            strides += [st[t_ax], st[h_ax], 0]
+        lse = torch.full((hq, total_q), float("nan"), device=q.device,
+                         dtype=torch.float32) if with_lse else None
+        ssq, ssk = seqstart_q.data_ptr(), seqstart_k.data_ptr()
+    arr = (ctypes.c_longlong * 12)(*[int(x) for x in strides])
+    rc = lib.gpu_ref_fmha_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                              lse.data_ptr() if lse is not None else None, arr, batch, hq, hk,
+                              sq, sk, int(causal), ssq, ssk, total_q, 1.0 / 8.0,
+                              ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"gpu_ref launch failed: CUDA error {rc}")
+    return o, lse
+
+
+def compare_device(o_kern, o_ref, lse_kern=None, lse_ref=None) -> dict:
+    """North-star verdict on device tensors (no host copy of the data):
+    max-abs and rel-L2 of O (kernel bf16 vs oracle fp32), LSE max |d| with
+    -inf == -inf; rows where the oracle is NaN are skipped."""
+    import torch
+
+    ref = o_ref.double()
+    ker = o_kern.double()
+    ok = ~torch.isnan(ref)
+    d = torch.where(ok, (ker - ref).abs(), torch.zeros_like(ref))
+    nonfinite = int((~torch.isfinite(ker) & ok).sum().item())
+    out = {"nonfinite": nonfinite, "max_abs": float(d.max().item())}
+    num = torch.sqrt((d * d).sum()).item()
+    den = torch.sqrt(torch.where(ok, ref * ref, torch.zeros_like(ref)).sum()).item()
+    out["rel_l2"] = num / den if den > 0 else num
+    out["baseline_pass"] = (nonfinite == 0 and out["max_abs"] <= BASE_TOL_MAX_ABS and
+                            out["rel_l2"] <= BASE_TOL_REL_L2)
+    if lse_kern is not None and lse_ref is not None:
+        lr = lse_ref.double()
+        lk = lse_kern.double()
+        sel = ~torch.isnan(lr)
+        both = torch.isneginf(lk) & torch.isneginf(lr)
+        dl = (lk - lr).abs()
+        dl = torch.where(both, torch.zeros_like(dl), dl)
+        dl = torch.where(torch.isnan(dl), torch.full_like(dl, float("inf")), dl)
+        dl = torch.where(sel, dl, torch.zeros_like(dl))
+        out["lse_max_abs"] = float(dl.max().item())
+        out["lse_pass"] = out["lse_max_abs"] <= LSE_TOL_ABS
+    return out

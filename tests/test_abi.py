@@ -103,3 +103,28 @@ def test_dense_entry_rejects_seqstart():
 def test_null_params_rejected():
     lib = fm.load_library()
     assert lib.fmha_fwd_d64_bf16(None, 1, 0, 0, 0, None) == fm.FMHA_ERR_ARG
+
+
+def test_valid_call_without_gpu_returns_a_status():
+    """A well-formed call on a machine without a usable sm_100 device goes
+    through validation and tensor-map encoding and returns FMHA_ERR_DEVICE
+    (never crashes); on a B200 this test is skipped (it would launch)."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: this call would launch on fake pointers")
+    p = _valid_params()
+    for causal in (False, True):
+        assert fm.call_entry(p, 1, causal, False) == fm.FMHA_ERR_DEVICE
+    tiles = (ctypes.c_int32 * 4)(0, 0, 1, 1)
+    lib = fm.load_library()
+    lib.fmha_fwd_d64_bf16_tiles_noalloc.argtypes = [
+        ctypes.POINTER(fm.FmhaFwdParams), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+    assert lib.fmha_fwd_d64_bf16_tiles_noalloc(ctypes.byref(p), 1, 0, 0, 0,
+                                               ctypes.cast(tiles, ctypes.c_void_p), 2,
+                                               None) == fm.FMHA_ERR_DEVICE
+    bad = (ctypes.c_int32 * 2)(5, 0)  # (batch, head) index outside B1 H2
+    assert lib.fmha_fwd_d64_bf16_tiles_noalloc(ctypes.byref(p), 1, 0, 0, 0,
+                                               ctypes.cast(bad, ctypes.c_void_p), 1,
+                                               None) == fm.FMHA_ERR_ARG
