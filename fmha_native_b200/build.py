@@ -96,8 +96,38 @@ def build_test_lib(force: bool = False) -> str | None:
     return TEST_LIB
 
 
+CPP_TEST_SRC = os.path.join(REPO_DIR, "tests", "cpp", "test_fmha_fwd_d64.cpp")
+CPP_TEST_BIN = os.path.join(REPO_DIR, "tests", "cpp", "test_fmha_fwd_d64")
+ORACLE_C = os.path.join(REPO_DIR, "oracle", "fmha_oracle.c")
+
+
+def build_cpp_tests(force: bool = False) -> str | None:
+    """The C++17 gtest-format parity suite (tests/cpp) over the C ABI, linked
+    with the C oracle; skipped when the tests tree is absent."""
+    if not os.path.exists(CPP_TEST_SRC):
+        return None
+    lib = build_library()
+    cpp_dir = os.path.dirname(CPP_TEST_SRC)
+    deps = [CPP_TEST_SRC, ORACLE_C, lib, os.path.join(cpp_dir, "mini_gtest.h"),
+            os.path.join(cpp_dir, "test_cases.inc"), os.path.join(REPO_DIR, "include", "fmha_fwd.h")]
+    if not force and not _stale(CPP_TEST_BIN, deps):
+        return CPP_TEST_BIN
+    cuda = os.path.dirname(os.path.dirname(nvcc_path()))
+    obj = CPP_TEST_BIN + ".oracle.o"
+    subprocess.run(["gcc", "-O2", "-fopenmp", "-std=c11", "-c", ORACLE_C, "-o", obj], check=True)
+    subprocess.run(["g++", "-std=c++17", "-O2", "-fopenmp", "-I", os.path.join(REPO_DIR, "include"),
+                    "-I", os.path.join(cuda, "include"), CPP_TEST_SRC, obj,
+                    "-o", CPP_TEST_BIN + ".tmp", "-L", PKG_DIR, "-lfmha_b200",
+                    f"-Wl,-rpath,{PKG_DIR}", "-Wl,-rpath,$ORIGIN/../../fmha_native_b200",
+                    "-L", os.path.join(cuda, "lib64"), "-lcudart", "-lm"], check=True)
+    os.replace(CPP_TEST_BIN + ".tmp", CPP_TEST_BIN)
+    os.remove(obj)
+    return CPP_TEST_BIN
+
+
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose="-v" in sys.argv)
     build_cli(force="--force" in sys.argv)
     build_test_lib(force="--force" in sys.argv)
+    build_cpp_tests(force="--force" in sys.argv)
     print(LIB_PATH)
