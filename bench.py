@@ -496,6 +496,84 @@ def cpu_baseline(w):
                 "sample": f"failed: {exc}"}
 
 
+SWEEP_SIZES = [(8, 16, 1024), (4, 16, 2048), (2, 16, 4096), (1, 8, 8192), (1, 16, 8192),
+               (1, 8, 16384), (1, 4, 32768), (1, 2, 40000)]  # run-benchmark.sh:12-21
+SWEEP_RUNS, SWEEP_DROP = 6, 1                                 # run-benchmark.sh:23-27
+
+
+def sweep(args):
+    """The reference's performance sweep (scripts/run-benchmark.sh of
+    poyenc/fmha_native) on the bench_fmha_fwd CLI: its 8 dense configs plus
+    the north-star varlen batch, each run SWEEP_RUNS times, the first dropped
+    and the rest averaged; with GPU-count, TFLOPS/GPU and %peak columns and the
+    reference's CPU oracle (oracle/_ref cpu_ref_verify) timed on a bounded
+    sample of each config on this host."""
+    import re
+
+    from fmha_native_b200 import build as kbuild
+    from fmha_native_b200.synth import varlen_lengths
+
+    cli = kbuild.build_cli()
+    peak_tf, _, peak_kind = load_peaks()
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    have_ref = O.have_reference() and not args.no_cpu_baseline
+    if have_ref:
+        os.environ["OMP_NUM_THREADS"] = str(host_cores())
+    rows = [("dense", b, h, s, None) for b, h, s in SWEEP_SIZES]
+    vl = varlen_lengths()
+    rows.append(("varlen", len(vl), 16, max(vl), vl))
+    print(f"Sweep: {len(rows)} configs, mask={args.mask}, gpus={args.gpus}, "
+          f"runs={SWEEP_RUNS} (drop {SWEEP_DROP}), peak {peak_tf} TFLOP/s ({peak_kind})")
+    hdr = (f"{'B':>4} {'H':>3} {'S':>6} {'D':>4} | {'Avg(ms)':>10} {'Min(ms)':>10} {'TFLOPS':>10} | "
+           f"{'GPUs':>4} {'TFLOPS/GPU':>10} {'%peak':>6} | {'CPU_ms':>9} {'CPU_threads':>11}")
+    print(hdr)
+    print("-" * len(hdr))
+    results = []
+    for kind, b, h, s, seqs in rows:
+        cmd = [cli, "-b", str(b), "-h", str(h), "-s", str(s), "-d", "64", "--mask", str(args.mask),
+               "--warmup", "5", "--iters", "20", "--gpus", str(args.gpus), "--peak", str(peak_tf)]
+        if seqs:
+            cmd += ["--varlen-seqs", ",".join(str(x) for x in seqs)]
+        vals = {"avg": [], "min": [], "tf": []}
+        err = None
+        for run in range(SWEEP_RUNS):
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                err = (r.stderr or r.stdout).strip().splitlines()[-1:] or [f"exit {r.returncode}"]
+                break
+            if run < SWEEP_DROP:
+                continue
+            vals["avg"].append(float(re.search(r"^Avg: ([0-9.]+)", r.stdout, re.M).group(1)))
+            vals["min"].append(float(re.search(r"^min=([0-9.]+)", r.stdout, re.M).group(1)))
+            vals["tf"].append(float(re.search(r"^TFLOPS: ([0-9.]+)", r.stdout, re.M).group(1)))
+        cpu_ms, cpu_thr = None, None
+        if have_ref and err is None:
+            from fmha_native_b200.synth import Workload
+
+            w = Workload("sweep", b, h, s, bool(args.mask), False,
+                         layout="thd" if seqs else "bshd", varlen_seqs=tuple(seqs) if seqs else None)
+            res = time_cpu_reference(O, cpu_sample(w), steps=1, warmup=0)
+            cpu_ms, cpu_thr = res["ms"], res["threads"]
+        if err is None:
+            avg = sum(vals["avg"]) / len(vals["avg"])
+            mn = min(vals["min"])
+            tf = sum(vals["tf"]) / len(vals["tf"])
+            line = (f"{b:>4} {h:>3} {s:>6} {64:>4} | {avg:>10.3f} {mn:>10.3f} {tf:>10.2f} | "
+                    f"{args.gpus:>4} {tf / args.gpus:>10.2f} {100 * tf / args.gpus / peak_tf:>6.1f} | "
+                    f"{cpu_ms if cpu_ms is None else round(cpu_ms, 1)!s:>9} {cpu_thr!s:>11}")
+            results.append({"kind": kind, "b": b, "h": h, "s": s, "mask": args.mask,
+                            "avg_ms": round(avg, 4), "min_ms": mn, "tflops": round(tf, 2),
+                            "gpus": args.gpus, "pct_peak": round(100 * tf / args.gpus / peak_tf, 2),
+                            "cpu_sample_ms": cpu_ms, "cpu_threads": cpu_thr})
+        else:
+            line = f"{b:>4} {h:>3} {s:>6} {64:>4} | ERROR: {err[0]}"
+        print(line, flush=True)
+    print(json.dumps({"sweep": results, "peak_tflops": peak_tf, "peak_kind": peak_kind}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -516,7 +594,12 @@ def main():
                     help="N>1: every rank runs its own copy of the workload (weak scaling)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch to report in roofline.traffic")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the reference's 8-config sweep (+ varlen) on the bench_fmha_fwd CLI")
+    ap.add_argument("--mask", type=int, default=0, help="--sweep: causal mask 0|1")
     args = ap.parse_args()
+    if args.sweep:
+        return sweep(args)
     if args.impl == "reference":
         return reference_arm(args, args.config)
     return native_arm(args, args.config)

@@ -134,6 +134,17 @@ struct KernelArgs {
     float* part_lse;           // split-KV partial LSE (natural log) [item][128]
 };
 
+struct TileWork {
+    int n;                      // KV tiles the query tile walks (from j0)
+    int j0;                     // first KV tile (split-KV ranges start past 0)
+    int row0;                   // first query row of the tile (sequence-local)
+    int seqlen_q, seqlen_k;
+    int off_q, off_k;           // varlen packed-row offsets
+    int b, h, kvh;
+    int x;                      // work-item index (split-KV workspace slot)
+    bool partial;               // split-KV item: partial O/LSE into the workspace
+};
+
 struct alignas(1024) SharedStorage {
     uint8_t q[2][kTileBytes];      // Q of the current and the next query tile
     uint8_t kv[kStages][kTileBytes];
@@ -147,6 +158,7 @@ struct alignas(1024) SharedStorage {
     uint64_t bar_pv;               // O += P V done (MMA commit)
     uint64_t bar_ofree;            // final O of a tile read out (128 arrivals)
     uint64_t bar_drain;
+    TileWork work[kSoftmaxWarps];  // softmax warps' current tile (see the softmax loop)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -180,16 +192,6 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const
     }
 }
 
-struct TileWork {
-    int n;                      // KV tiles the query tile walks (from j0)
-    int j0;                     // first KV tile (split-KV ranges start past 0)
-    int row0;                   // first query row of the tile (sequence-local)
-    int seqlen_q, seqlen_k;
-    int off_q, off_k;           // varlen packed-row offsets
-    int b, h, kvh;
-    int x;                      // work-item index (split-KV workspace slot)
-    bool partial;               // split-KV item: partial O/LSE into the workspace
-};
 
 // Work item x of the launch -> query tile and KV range.  Returns false for an
 // item that computes nothing (a query block past the end of its sequence,
@@ -606,16 +608,27 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         const float scale = a.scale;
         bool ok = true;
         int g = 0;      // flat KV step counter
-        TileWork w;
+        // The tile description is parked in shared memory (one copy per warp)
+        // while the KV loop runs, so its fields hold no registers there; the
+        // loop itself needs only the scalars below.
+        TileWork* wsave = &sm.work[warp];
         for (int k = 0; ok; ++k) {
             const int x = work_index(a, k);
             if (x == -1) break;
-            if (x < 0 || !decode_work<kCausal, kVarlen>(a, x, w)) continue;
-            const int n = w.n;
-            const int row = w.row0 + t;
-            const int shift = w.seqlen_k - w.seqlen_q;
-            // Keys visible to this row: [0, key_lim).
-            const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
+            int n, k0, tile_lim, key_lim;
+            {
+                TileWork w;
+                if (x < 0 || !decode_work<kCausal, kVarlen>(a, x, w)) continue;
+                n = w.n;
+                k0 = w.j0 * kBlockN;
+                const int shift = w.seqlen_k - w.seqlen_q;
+                // Keys visible to this row: [0, key_lim); a KV tile needs the
+                // mask once it reaches past the smallest limit of its rows.
+                key_lim = kCausal ? min(w.seqlen_k, w.row0 + t + shift + 1) : w.seqlen_k;
+                tile_lim = kCausal ? min(w.seqlen_k, w.row0 + shift + 1) : w.seqlen_k;
+                if (lane == 0) *wsave = w;
+                __syncwarp();
+            }
 
             float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
             float l_run = 0.0f;       // running sum of un-normalised P
@@ -639,9 +652,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 tc_fence_before();
                 mbar_arrive(smem_u32(&sm.bar_sfree));
 
-                const int k0 = (w.j0 + j) * kBlockN;
-                const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
-                                       (kCausal && k0 + kBlockN - 1 > w.row0 + shift);
+                const bool need_mask = k0 + kBlockN > tile_lim;
                 if (need_mask) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c)
@@ -649,6 +660,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                         for (int e = 0; e < 32; ++e)
                             if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
                 }
+                k0 += kBlockN;
                 // Row max: 8 independent 3-input-max chains.
                 float mx[8];
 #pragma unroll
@@ -766,6 +778,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 tc_fence_before();
                 mbar_arrive(smem_u32(&sm.bar_ofree));
             }
+            __syncwarp();
+            const TileWork w = *wsave;
+            __syncwarp();  // every lane has its copy before the next tile's write
             store_row<kVarlen>(a, w, t, o, n > 0, m_run, l_run);
         }
     }
