@@ -53,7 +53,6 @@ ENTRY_POINTS = (
     "fmha_fwd_d64_items_workspace_bytes",
     "fmha_fwd_d64_status",
     "fmha_fwd_d64_set_wait_limit_ns",
-    "fmha_fwd_d64_set_max_ctas",
     "fmha_fwd_d64_release",
     "fmha_fwd_d64_error_string",
 )
@@ -129,8 +128,6 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fmha_fwd_d64_status.restype = ctypes.c_int
     lib.fmha_fwd_d64_set_wait_limit_ns.argtypes = [ctypes.c_ulonglong]
     lib.fmha_fwd_d64_set_wait_limit_ns.restype = None
-    lib.fmha_fwd_d64_set_max_ctas.argtypes = [ctypes.c_int]
-    lib.fmha_fwd_d64_set_max_ctas.restype = None
     lib.fmha_fwd_d64_release.argtypes = []
     lib.fmha_fwd_d64_release.restype = None
     lib.fmha_fwd_d64_error_string.argtypes = [ctypes.c_int]

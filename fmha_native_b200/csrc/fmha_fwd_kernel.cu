@@ -1,36 +1,38 @@
 // fmha_fwd_kernel.cu -- B200 (sm_100a) head-dim-64 BF16 fused attention
 // forward, and the C-ABI launchers declared in include/fmha_fwd.h.
 //
-// A persistent CTA loops over 128-row query tiles of (batch, head) pairs
-// (work items dealt out in rounds, alternating direction) and walks each
-// tile's key/value sequence in 128-key tiles; two CTAs share each SM, each
-// with its own pipeline.  The CTA is warp specialised:
+// One CTA owns one 128-row query tile of one (batch, head) and walks the
+// key/value sequence in 128-key tiles; two CTAs share each SM, each with its
+// own pipeline.  The CTA is warp specialised:
 //
-//   warps 0-3  softmax + epilogue : one query row per thread (TMEM lane = row)
-//   warp  4    TMA producer       : Q of the current and next tile (double
-//                                   buffer), K_j / V_j into a 4-slot ring
-//   warp  5    MMA issuer         : one elected lane issues every tcgen05.mma;
-//                                   the warp also owns the TMEM allocation
-//   warps 6-7  idle               : complete the control warpgroup for setmaxnreg
+//   warps 0-3  softmax          : one query row per thread (TMEM lane = row)
+//   warp  4    TMA producer     : Q once, then K_j / V_j into a 4-slot ring
+//   warp  5    MMA issuer       : one elected lane issues every tcgen05.mma;
+//                                 the warp also owns the TMEM allocation
+//   warps 6-7  idle             : complete the control warpgroup for setmaxnreg
 //
 // Tensor memory (256 columns x 128 lanes per CTA; two CTAs fill the SM):
 //   [  0,128) S = Q K^T (fp32)
 //   [128,192) O accumulator (fp32)
 //   [192,256) P (bf16x2)
 //
-// The pipeline is one flat stream of KV steps g across the CTA's tiles:
-//   MMA : S(g) = Q K^T -> commit(s_full)
+// Per KV tile j the schedule is
+//   MMA : S = Q K_j^T -> commit(s_full)
 //   SM  : S -> registers -> arrive(s_free) -> mask, row max, (lazy) rescale
-//         of O -> P = exp2(S*scale - m*scale) -> wait(pv_done(g-1)) ->
+//         of O -> P = exp2(S*scale - m*scale) -> wait(pv_done of j-1) ->
 //         bf16 P into TMEM -> arrive(p_full)
-//   MMA : S(g+1) as soon as s_free arrives (also when g+1 starts the next
-//         tile), then O += P(g) V(g) -> commit(pv_done)
-//   SM  : after a tile's last step: wait(pv_done), O -> registers ->
-//         arrive(o_free) -> O/l and LSE to global memory; the MMA warp starts
-//         the next tile's first P V only after o_free.
-// tcgen05 MMAs issued by one thread execute in order, so pv_done(g-1) also
+//   MMA : S = Q K_{j+1}^T as soon as s_free arrives, then O += P V_j ->
+//         commit(pv_done)
+// tcgen05 MMAs issued by one thread execute in order, so pv_done(j-1) also
 // proves every earlier MMA finished, which is what makes the softmax-side O
 // rescale race free.
+//
+// CTAs start in work order (heaviest query tiles first inside L2-sized head
+// groups), so the hardware block scheduler balances the load dynamically.  A
+// persistent variant (two resident CTAs per SM looping over the tiles, Q
+// double-buffered, the next tile's first QK^T issued before the current
+// tile's last PV) measured 4-8 % slower on every north-star shape: the
+// neighbouring CTA already hides one CTA's start and finish.
 //
 // Reference semantics followed (poyenc/fmha_native):
 //   grid decode + causal heavy-first order ... src/fused/kernel.cpp:55-99
@@ -66,10 +68,17 @@ namespace {
 constexpr int kBlockM = 128;            // rows per query tile
 constexpr int kBlockN = 128;            // keys per KV tile
 constexpr int kHeadDim = 64;
-constexpr int kCtasPerSm = 2;           // two independent persistent CTAs per SM
+// One CTA = one 128-row query tile (128 query rows, 256 threads, 256 TMEM
+// columns, ~80 KB shared memory); two CTAs run per SM, each with its own
+// pipeline, fully independent of its neighbour.  The per-tile arrays and
+// loops below run over that one tile.
+constexpr int kTilesPerCta = 1;
+constexpr int kRowsPerCta = kBlockM * kTilesPerCta;
+constexpr int kCtasPerSm = 2;
 constexpr int kStages = 4;              // K/V ring slots (K_j, V_j alternate)
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB (Q, K or V tile)
-constexpr int kSoftmaxWarps = 4;        // one thread per query row
+constexpr int kWarpsPerTile = 4;   // softmax warps per query tile: one thread per row
+constexpr int kSoftmaxWarps = kWarpsPerTile * kTilesPerCta;
 constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax group + control group
 // Register split (setmaxnreg): the CTA launches with kThreads x kLaunchRegs
 // registers; the softmax group takes kRegsSoftmax, the producer/MMA group
@@ -77,14 +86,16 @@ constexpr int kThreads = 32 * kSoftmaxWarps + 128;  // softmax group + control g
 constexpr int kRegsSoftmax = 192;
 constexpr int kRegsControl = 64;
 constexpr int kLaunchRegs = 128;
-static_assert(128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs,
+static_assert(32 * kSoftmaxWarps * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs,
               "setmaxnreg split exceeds the launch register pool");
 constexpr int kWarpLoad = kSoftmaxWarps;
 constexpr int kWarpMma = kSoftmaxWarps + 1;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColS = 0;    // S = Q K^T (fp32), 128 columns
-constexpr uint32_t kColO = 128;  // O accumulator (fp32), 64 columns
-constexpr uint32_t kColP = 192;  // P (bf16x2), 64 columns
+constexpr uint32_t kTmemCols = 256 * kTilesPerCta;
+__host__ __device__ constexpr uint32_t col_s(int i) { return i * 128u; }        // S_i (fp32)
+__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * kTilesPerCta + i * 64u; }  // O_i
+__host__ __device__ constexpr uint32_t col_p(int i) {  // P_i (bf16x2)
+    return 192u * kTilesPerCta + i * 64u;
+}
 // Lazy rescale threshold in log2 units: the running max is only moved when
 // it grows by more than this, bounding un-normalised P by 2^8.
 constexpr float kRescaleThreshold = 8.0f;
@@ -115,6 +126,7 @@ struct KernelArgs {
     float* lse;
     const int32_t* seqstart_q;
     const int32_t* seqstart_k;
+    const int32_t* seq_order;  // varlen launch order: slot -> sequence, longest first (or null)
     long long stride_o, nhead_stride_o, batch_stride_o;
     int seqlen_q, seqlen_k;
     int nhead_q, nhead_k;
@@ -123,7 +135,6 @@ struct KernelArgs {
     int* err_word;
     unsigned long long wait_limit_ns;
     int stall_inject;          // test hook: producer withholds the first V tile
-    int n_work;                // work items of the launch (CTAs loop over them)
     const int32_t* tiles;      // optional work list of (b*nhead_q+h, query block)
     int m_blocks;              // query blocks per (batch, head) in a full launch
     int head_group;            // (batch, head) pairs per L2 group of the launch order
@@ -134,31 +145,18 @@ struct KernelArgs {
     float* part_lse;           // split-KV partial LSE (natural log) [item][128]
 };
 
-struct TileWork {
-    int n;                      // KV tiles the query tile walks (from j0)
-    int j0;                     // first KV tile (split-KV ranges start past 0)
-    int row0;                   // first query row of the tile (sequence-local)
-    int seqlen_q, seqlen_k;
-    int off_q, off_k;           // varlen packed-row offsets
-    int b, h, kvh;
-    int x;                      // work-item index (split-KV workspace slot)
-    bool partial;               // split-KV item: partial O/LSE into the workspace
-};
-
 struct alignas(1024) SharedStorage {
-    uint8_t q[2][kTileBytes];      // Q of the current and the next query tile
+    uint8_t q[kTilesPerCta][kTileBytes];
     uint8_t kv[kStages][kTileBytes];
-    uint64_t bar_qfull[2];
-    uint64_t bar_qempty[2];        // Q buffer's last S issued and done (MMA commit)
+    uint64_t bar_q[kTilesPerCta];
     uint64_t bar_full[kStages];
     uint64_t bar_empty[kStages];
-    uint64_t bar_s;                // S written (MMA commit)
-    uint64_t bar_sfree;            // S read into registers (128 arrivals)
-    uint64_t bar_p;                // P written, O rescaled (128 arrivals)
-    uint64_t bar_pv;               // O += P V done (MMA commit)
-    uint64_t bar_ofree;            // final O of a tile read out (128 arrivals)
+    uint64_t bar_s[kTilesPerCta];      // S_i written (MMA commit)
+    uint64_t bar_sfree[kTilesPerCta];  // S_i read into registers (128 arrivals)
+    uint64_t bar_p[kTilesPerCta];      // P_i written, O_i rescaled (128 arrivals)
+    uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
+    uint64_t bar_o[kTilesPerCta];
     uint64_t bar_drain;
-    TileWork work[kSoftmaxWarps];  // softmax warps' current tile (see the softmax loop)
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -192,17 +190,23 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity, const
     }
 }
 
+struct TileWork {
+    int n_kv[kTilesPerCta];     // KV tiles each query tile walks (from j0)
+    int j0;                     // first KV tile (split-KV ranges start past 0)
+    int row0;                   // first query row of the CTA (sequence-local)
+    int seqlen_q, seqlen_k;
+    int off_q, off_k;           // varlen packed-row offsets
+    int b, h, kvh;
+    bool partial;               // split-KV item: partial O/LSE into the workspace
+};
 
-// Work item x of the launch -> query tile and KV range.  Returns false for an
-// item that computes nothing (a query block past the end of its sequence,
-// or a malformed work-list entry, which is skipped without any access).
 template <bool kCausal, bool kVarlen>
-__device__ __forceinline__ bool decode_work(const KernelArgs& a, int x, TileWork& w) {
+__device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
     int hb, mblk;
     int split = 0;
     int kv_begin = 0, kv_end = -1;  // work items: explicit KV-tile range (end < 0: all)
     if (a.items != nullptr) {
-        const int4 it = reinterpret_cast<const int4*>(a.items)[x];
+        const int4 it = reinterpret_cast<const int4*>(a.items)[blockIdx.x];
         hb = it.x;
         mblk = it.y;
         kv_begin = it.z;
@@ -211,31 +215,34 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, int x, TileWork
     } else if (a.tiles != nullptr) {
         // Caller-supplied work list: (batch*nhead_q + head, query block); in
         // split-KV mode every entry expands into num_splits KV ranges.
-        const int e = a.num_splits > 1 ? x / a.num_splits : x;
-        if (a.num_splits > 1) split = x - e * a.num_splits;
-        hb = a.tiles[2 * e];
-        mblk = a.tiles[2 * e + 1];
+        const int x = a.num_splits > 1 ? (int)blockIdx.x / a.num_splits : (int)blockIdx.x;
+        if (a.num_splits > 1) split = (int)blockIdx.x % a.num_splits;
+        hb = a.tiles[2 * x];
+        mblk = a.tiles[2 * x + 1];
     } else {
         // Launch order: (batch, head) pairs in groups of head_group whose K/V
         // fit in L2 together; inside a group causal blocks go heaviest first
         // across all its heads (src/fused/kernel.cpp:73,96), so the group's
         // K/V is read from HBM about once.
         const int mb = a.m_blocks;
-        const int g = x / (a.head_group * mb);
-        const int r = x - g * a.head_group * mb;
+        const int lin = blockIdx.x;
+        const int g = lin / (a.head_group * mb);
+        const int r = lin - g * a.head_group * mb;
         const int gs = min(a.head_group, a.num_hb - g * a.head_group);
         hb = g * a.head_group + r % gs;
         const int mrank = r / gs;
         mblk = kCausal ? mb - 1 - mrank : mrank;
     }
     // A list entry naming no (batch, head) of the problem, or a negative or
-    // out-of-range query block, is skipped before any address is formed.
+    // out-of-range query block, computes nothing and forms no address.
     if (hb < 0 || hb >= a.num_hb || mblk < 0 || mblk >= a.m_blocks) return false;
-    w.x = x;
     w.h = hb % a.nhead_q;
     w.b = hb / a.nhead_q;
     w.kvh = w.h / (a.nhead_q / a.nhead_k);
     if constexpr (kVarlen) {
+        // Full varlen launch: batch slots are walked longest sequence first.
+        if (a.seq_order != nullptr && a.tiles == nullptr && a.items == nullptr)
+            w.b = a.seq_order[w.b];
         w.off_q = a.seqstart_q[w.b];
         w.off_k = a.seqstart_k[w.b];
         w.seqlen_q = a.seqstart_q[w.b + 1] - w.off_q;
@@ -249,42 +256,43 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, int x, TileWork
         w.seqlen_q = a.seqlen_q;
         w.seqlen_k = a.seqlen_k;
     }
-    w.row0 = mblk * kBlockM;
+    w.row0 = mblk * kRowsPerCta;
     if (w.row0 >= w.seqlen_q) return false;
     const int shift = w.seqlen_k - w.seqlen_q;  // bottom-right causal alignment
-    int kend = w.seqlen_k;
-    if (kCausal) {
-        const int r_last = min(w.row0 + kBlockM - 1, w.seqlen_q - 1);
-        kend = min(w.seqlen_k, r_last + shift + 1);
+#pragma unroll
+    for (int i = 0; i < kTilesPerCta; ++i) {
+        const int r0 = w.row0 + i * kBlockM;
+        if (r0 >= w.seqlen_q) {
+            w.n_kv[i] = 0;
+            continue;
+        }
+        int kv_end = w.seqlen_k;
+        if (kCausal) {
+            const int r_last = min(r0 + kBlockM - 1, w.seqlen_q - 1);
+            kv_end = min(w.seqlen_k, r_last + shift + 1);
+        }
+        w.n_kv[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
     }
-    w.n = kend > 0 ? (kend + kBlockN - 1) / kBlockN : 0;
     w.j0 = 0;
     w.partial = a.num_splits > 1 || (a.items != nullptr && kv_end >= 0);
     if (a.items != nullptr && kv_end >= 0) {
-        w.n = max(0, min(w.n, kv_end) - kv_begin);
-        w.j0 = kv_begin;
-    } else if (a.num_splits > 1) {
-        // KV range of this split: an equal share of the tile's range.
-        const int chunk = (w.n + a.num_splits - 1) / a.num_splits;
-        const int jb = split * chunk;
-        const int je = min(w.n, jb + chunk);
+        const int jb = max(0, kv_begin);
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], kv_end) - jb);
         w.j0 = jb;
-        w.n = max(0, je - jb);
+    } else if (a.num_splits > 1) {
+        // KV range of this split: an equal share of the longer tile's range.
+        int n_all = 0;
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) n_all = max(n_all, w.n_kv[i]);
+        const int chunk = (n_all + a.num_splits - 1) / a.num_splits;
+        const int jb = split * chunk;
+        const int je = min(n_all, jb + chunk);
+        w.j0 = jb;
+#pragma unroll
+        for (int i = 0; i < kTilesPerCta; ++i) w.n_kv[i] = max(0, min(w.n_kv[i], je) - jb);
     }
     return true;
-}
-
-// k-th work item of this CTA: items are dealt out in rounds of gridDim.x,
-// alternately in CTA order and in reverse ("snake"), so a list sorted
-// heaviest first spreads its heavy and light items evenly over the CTAs.
-// Returns -1 past the end of the list, -2 for a hole in the last round.
-__device__ __forceinline__ int work_index(const KernelArgs& a, int k) {
-    const int g = (int)gridDim.x;
-    const long long base = (long long)k * g;
-    if (base >= a.n_work) return -1;
-    const int c = (int)blockIdx.x;
-    const long long x = base + ((k & 1) ? (g - 1 - c) : c);
-    return x < a.n_work ? (int)x : -2;
 }
 
 template <bool kVarlen>
@@ -301,78 +309,6 @@ __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* t
     }
 }
 
-// Output of one query row: O * (1/l) rounded to bf16 and the LSE (dense or
-// varlen layouts), or for a split-KV item the normalised fp32 partial O and
-// its LSE in the workspace.  `o` holds the row's 64 fp32 accumulator columns
-// (zeros when the tile visited no key: the row is O = 0, LSE = -inf,
-// src/fused/pipeline.hpp:207-222).
-template <bool kVarlen>
-__device__ __forceinline__ void store_row(const KernelArgs& a, const TileWork& w, int t,
-                                          const uint32_t (&o)[2][32], bool any_key, float m_run,
-                                          float l_run) {
-    const int row = w.row0 + t;
-    const float inv_l = (any_key && l_run > 0.0f) ? 1.0f / l_run : 0.0f;
-    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-    const float lse = (any_key && l_run > 0.0f)
-                          ? (__log2f(l_run) + m_use * a.scale - kPLog2Bias) * 0.69314718055994531f
-                          : -INFINITY;
-    if (w.partial) {
-        const size_t prow = (size_t)w.x * kBlockM + t;
-        float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim);
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            float v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = c * 4 + e;
-                v[e] = __uint_as_float(o[col >> 5][col & 31]) * inv_l;
-            }
-            dst[c] = make_float4(v[0], v[1], v[2], v[3]);
-        }
-        a.part_lse[prow] = lse;
-        return;
-    }
-    if (row >= w.seqlen_q) return;
-    uint16_t* orow;
-    if constexpr (kVarlen) {
-        orow = a.o + (long long)w.h * a.nhead_stride_o + (long long)(w.off_q + row) * a.stride_o;
-    } else {
-        orow = a.o + (long long)w.b * a.batch_stride_o + (long long)w.h * a.nhead_stride_o +
-               (long long)row * a.stride_o;
-    }
-    uint4* dst = reinterpret_cast<uint4*>(orow);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int col = c * 8 + e * 2;
-            const float v0 = __uint_as_float(o[col >> 5][col & 31]) * inv_l;
-            const float v1 = __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l;
-#ifdef FMHA_O_ROUND_TRUNC
-            pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
-#else
-            pk[e] = pack_bf16_rne(v0, v1);
-#endif
-        }
-        dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-    if (a.lse != nullptr) {
-        long long idx;
-        if constexpr (kVarlen) {
-            idx = (long long)w.h * a.total_q + w.off_q + row;
-        } else {
-            idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
-        }
-        a.lse[idx] = lse;
-    }
-}
-
-// Persistent CTA: loops over the work items work_index(k), k = 0, 1, ...
-// Every role walks the same item sequence; the pipeline runs on as one flat
-// stream of KV steps across query tiles (step counter g), so the first S of
-// the next tile is computed while the softmax finishes the current one, and
-// the next tile's Q is loaded (double buffer) while the current one runs.
 template <bool kCausal, bool kVarlen>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
@@ -380,20 +316,22 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     SharedStorage& sm = *reinterpret_cast<SharedStorage*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
+    TileWork w;
+    if (!decode_work<kCausal, kVarlen>(a, w)) return;  // CTA-uniform early out
+
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     volatile int* abort_flag = &sm.abort_flag;
 
     if (threadIdx.x == 0) {
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(smem_u32(&sm.bar_qfull[b]), 1);
-            mbar_init(smem_u32(&sm.bar_qempty[b]), 1);
+        for (int i = 0; i < kTilesPerCta; ++i) {
+            mbar_init(smem_u32(&sm.bar_q[i]), 1);
+            mbar_init(smem_u32(&sm.bar_s[i]), 1);
+            mbar_init(smem_u32(&sm.bar_sfree[i]), 32 * kWarpsPerTile);
+            mbar_init(smem_u32(&sm.bar_p[i]), 32 * kWarpsPerTile);
+            mbar_init(smem_u32(&sm.bar_pv[i]), 1);
+            mbar_init(smem_u32(&sm.bar_o[i]), 1);
         }
-        mbar_init(smem_u32(&sm.bar_s), 1);
-        mbar_init(smem_u32(&sm.bar_sfree), 128);
-        mbar_init(smem_u32(&sm.bar_p), 128);
-        mbar_init(smem_u32(&sm.bar_pv), 1);
-        mbar_init(smem_u32(&sm.bar_ofree), 128);
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&sm.bar_full[s]), 1);
             mbar_init(smem_u32(&sm.bar_empty[s]), 1);
@@ -411,17 +349,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
-    // Next item of this CTA with at least one KV tile, from round *k on.
-    auto next_tile = [&](int& k, TileWork& w) -> bool {
-        for (;; ++k) {
-            const int x = work_index(a, k);
-            if (x == -1) return false;
-            if (x >= 0 && decode_work<kCausal, kVarlen>(a, x, w) && w.n > 0) {
-                ++k;
-                return true;
-            }
-        }
-    };
+    // Per-tile KV counts as scalars (a runtime-indexed array would live in
+    // local memory).
+    const int n_kv0 = w.n_kv[0];
+    const int n_kv1 = kTilesPerCta > 1 ? w.n_kv[kTilesPerCta - 1] : 0;
+    auto n_kv = [n_kv0, n_kv1](int i) { return i == 0 ? n_kv0 : n_kv1; };
+    const int n_max = max(n_kv0, n_kv1);
 
     if (warp >= kSoftmaxWarps) {
     regs_dec<kRegsControl>();
@@ -433,66 +366,46 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tma_prefetch_desc(&a.tm_v);
             const uint64_t pol_q = l2_policy_evict_first();
             const uint64_t pol_kv = l2_policy_evict_last();
-            int q_issued = 0;  // Q loads issued (tile count)
-            int issued = 0;    // K/V loads issued into the ring
-            bool ok = true;
-            auto issue_q = [&](const TileWork& w) -> bool {
-                const int b = q_issued & 1;
-                if (q_issued >= 2 &&
-                    !wait_phase(smem_u32(&sm.bar_qempty[b]), ((q_issued - 2) >> 1) & 1,
-                                abort_flag, a, kErrTimeoutLoad))
-                    return false;
-                const uint32_t bar = smem_u32(&sm.bar_qfull[b]);
+            const int qbatch = kVarlen ? 0 : w.b;
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (n_kv(i) == 0) continue;
+                const uint32_t bar = smem_u32(&sm.bar_q[i]);
                 mbar_arrive_expect_tx(bar, kTileBytes);
-                tma_load_rows<kVarlen>(smem_u32(sm.q[b]), &a.tm_q, bar, w.off_q + w.row0, w.h,
-                                       kVarlen ? 0 : w.b, pol_q);
-                ++q_issued;
-                return true;
-            };
-            int k = 0;
-            TileWork cur, nxt;
-            bool have_cur = next_tile(k, cur);
-            if (have_cur) ok = issue_q(cur);
-            int gstep = 0;  // flat KV step counter (for the stall test hook)
-            while (have_cur && ok) {
-                const bool have_nxt = next_tile(k, nxt);
-                for (int j = 0; j < cur.n && ok; ++j, ++gstep) {
-                    for (int kv = 0; kv < 2; ++kv) {
-                        const int idx = issued;
-                        const int slot = idx % kStages;
-                        const uint32_t use = idx / kStages;
-                        if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag,
-                                        a, kErrTimeoutLoad)) {
-                            ok = false;
-                            break;
-                        }
-                        if (a.stall_inject && gstep == 0 && kv == 1) {
-                            // Test hook: never deliver V_0, so the MMA warp's wait
-                            // runs out and the abort path is exercised without
-                            // any fault.
-                            ok = false;
-                            break;
-                        }
-                        const uint32_t bar = smem_u32(&sm.bar_full[slot]);
-                        mbar_arrive_expect_tx(bar, kTileBytes);
-                        tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), kv ? &a.tm_v : &a.tm_k,
-                                               bar, cur.off_k + (cur.j0 + j) * kBlockN, cur.kvh,
-                                               kVarlen ? 0 : cur.b, pol_kv);
-                        issued = idx + 1;
-                    }
-                    // The next tile's Q goes out once this tile's first K/V is
-                    // on its way.
-                    if (ok && j == 0 && have_nxt) ok = issue_q(nxt);
+                tma_load_rows<kVarlen>(smem_u32(sm.q[i]), &a.tm_q, bar,
+                                       w.off_q + w.row0 + i * kBlockM, w.h, qbatch, pol_q);
+            }
+            int issued = 0;  // loads issued into the ring
+            bool ok = true;
+            const int n_loads = 2 * n_max;
+            for (int idx = 0; idx < n_loads; ++idx) {
+                const int slot = idx % kStages;
+                const uint32_t use = idx / kStages;
+                if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag, a,
+                                kErrTimeoutLoad)) {
+                    ok = false;
+                    break;
                 }
-                cur = nxt;
-                have_cur = have_nxt;
+                if (a.stall_inject && idx == 1) {
+                    // Test hook: never deliver V_0, so the MMA warp's wait runs
+                    // out and the abort path is exercised without any fault.
+                    continue;
+                }
+                const uint32_t bar = smem_u32(&sm.bar_full[slot]);
+                mbar_arrive_expect_tx(bar, kTileBytes);
+                const CUtensorMap* tm = (idx & 1) ? &a.tm_v : &a.tm_k;
+                tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), tm, bar,
+                                       w.off_k + (w.j0 + (idx >> 1)) * kBlockN, w.kvh,
+                                       kVarlen ? 0 : w.b, pol_kv);
+                issued = idx + 1;
             }
             if (!ok || *abort_flag) {
                 // Let every copy this warp started land before the CTA exits.
-                for (int t = max(0, q_issued - 2); t < q_issued; ++t)
-                    drain_phase(smem_u32(&sm.bar_qfull[t & 1]), (t >> 1) & 1, a);
-                for (int idx = max(0, issued - kStages); idx < issued; ++idx)
+                for (int i = 0; i < kTilesPerCta; ++i)
+                    if (n_kv(i) > 0) drain_phase(smem_u32(&sm.bar_q[i]), 0, a);
+                for (int idx = max(0, issued - kStages); idx < issued; ++idx) {
+                    if (a.stall_inject && idx == 1) continue;
                     drain_phase(smem_u32(&sm.bar_full[idx % kStages]), (idx / kStages) & 1, a);
+                }
             }
         }
         __syncwarp();
@@ -522,12 +435,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         auto commit = [&](uint64_t* bar) {
             if (leader) mma_commit(smem_u32(bar));
         };
-        // S = Q K^T : M=128, N=128, K=64 as 4 x K16, 32 bytes (descriptor +2)
-        // apart inside the 128-byte swizzled rows.
-        auto issue_s = [&](int qb, int slot) {
-            const uint64_t da = dq0 + (uint64_t)(qb * (kTileBytes >> 4));
+        // S_i = Q_i K^T : M=128, N=128, K=64 as 4 x K16, 32 bytes (descriptor
+        // +2) apart inside the 128-byte swizzled rows.
+        auto issue_s = [&](int i, int slot) {
+            const uint64_t da = dq0 + (uint64_t)(i * (kTileBytes >> 4));
             const uint64_t db = dk0 + (uint64_t)(slot * (kTileBytes >> 4));
-            const uint32_t d = tmem + kColS;
+            const uint32_t d = tmem + col_s(i);
             if (leader) {
                 mma_ss(d, da, db, idesc_qk, 0u);
                 mma_ss(d, da + 2, db + 2, idesc_qk, 1u);
@@ -535,13 +448,13 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 mma_ss(d, da + 6, db + 6, idesc_qk, 1u);
             }
         };
-        // O += P V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the TMEM A
-        // operand; V is MN-major in shared memory, 16 keys = two 8-row
+        // O_i += P_i V : M=128, N=64, K=128 as 8 x K16.  P (bf16x2) is the
+        // TMEM A operand; V is MN-major in shared memory, 16 keys = two 8-row
         // swizzle atoms = 2048 bytes (descriptor +128) per step.
-        auto issue_pv = [&](int slot, bool accumulate) {
+        auto issue_pv = [&](int i, int slot, bool accumulate) {
             const uint64_t db = dv0 + (uint64_t)(slot * (kTileBytes >> 4));
-            const uint32_t d = tmem + kColO;
-            const uint32_t pa = tmem + kColP;
+            const uint32_t d = tmem + col_o(i);
+            const uint32_t pa = tmem + col_p(i);
             if (leader) {
                 mma_ts(d, pa, db, idesc_pv, accumulate ? 1u : 0u);
 #pragma unroll
@@ -549,49 +462,57 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     mma_ts(d, pa + kk * 8, db + (uint64_t)(kk * 128), idesc_pv, 1u);
             }
         };
-        // O += P(g) V(g) of flat step g; `first` starts a tile (O overwritten,
-        // after the previous tile's O was read out), tile = its tile count.
-        auto step_pv = [&](int g, bool first, int tile) -> bool {
-            const int v_idx = 2 * g + 1;
-            if (!wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx))) return false;
-            if (!wait_all(&sm.bar_p, g & 1)) return false;
-            if (first && tile > 0 && !wait_all(&sm.bar_ofree, (tile - 1) & 1)) return false;
-            tc_fence_after();
-            issue_pv(slot_of(v_idx), !first);
-            commit(&sm.bar_pv);
-            commit(&sm.bar_empty[slot_of(v_idx)]);
-            return true;
-        };
 
-        int k = 0;
-        int g = 0;      // flat KV step counter
-        int tile = 0;   // tiles with work seen by this CTA
-        int pend_g = -1, pend_tile = 0;
-        bool pend_first = false;
-        TileWork w;
-        while (ok && next_tile(k, w)) {
-            const int qb = tile & 1;
-            ok = wait_all(&sm.bar_qfull[qb], (tile >> 1) & 1);
-            for (int j = 0; j < w.n && ok; ++j, ++g) {
-                // S(g) as soon as the softmax has read S(g-1) and K landed ...
-                const int k_idx = 2 * g;
-                ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
-                if (ok && g > 0) ok = wait_all(&sm.bar_sfree, (g - 1) & 1);
+        for (int i = 0; i < kTilesPerCta && ok; ++i)
+            if (n_kv(i) > 0) ok = wait_all(&sm.bar_q[i], 0);
+        if (ok && n_max > 0) {
+            ok = wait_all(&sm.bar_full[slot_of(0)], full_parity(0));
+            if (ok) {
+                tc_fence_after();
+                for (int i = 0; i < kTilesPerCta; ++i) {
+                    if (n_kv(i) == 0) continue;
+                    issue_s(i, slot_of(0));
+                    commit(&sm.bar_s[i]);
+                }
+                commit(&sm.bar_empty[slot_of(0)]);
+            }
+        }
+        // Steady state, per KV tile j:
+        //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
+        //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
+        for (int j = 0; j < n_max && ok; ++j) {
+            const int v_idx = 2 * j + 1;
+            const int k_idx = 2 * j + 2;
+            bool k_used = false;
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (j + 1 >= n_kv(i)) continue;
+                if (!k_used) {
+                    ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
+                    if (!ok) break;
+                    k_used = true;
+                }
+                ok = wait_all(&sm.bar_sfree[i], j & 1);
                 if (!ok) break;
                 tc_fence_after();
-                issue_s(qb, slot_of(k_idx));
-                commit(&sm.bar_s);
-                commit(&sm.bar_empty[slot_of(k_idx)]);
-                if (j == w.n - 1) commit(&sm.bar_qempty[qb]);
-                // ... then O += P(g-1) V(g-1) once P(g-1) is written.
-                if (pend_g >= 0) ok = step_pv(pend_g, pend_first, pend_tile);
-                pend_g = g;
-                pend_first = (j == 0);
-                pend_tile = tile;
+                issue_s(i, slot_of(k_idx));
+                commit(&sm.bar_s[i]);
             }
-            ++tile;
+            if (!ok) break;
+            if (k_used) commit(&sm.bar_empty[slot_of(k_idx)]);
+            ok = wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx));
+            if (!ok) break;
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (j >= n_kv(i)) continue;
+                ok = wait_all(&sm.bar_p[i], j & 1);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(i, slot_of(v_idx), j > 0);
+                commit(&sm.bar_pv[i]);
+                if (j == n_kv(i) - 1) commit(&sm.bar_o[i]);
+            }
+            if (!ok) break;
+            commit(&sm.bar_empty[slot_of(v_idx)]);
         }
-        if (ok && pend_g >= 0) ok = step_pv(pend_g, pend_first, pend_tile);
         // All MMAs this warp issued must finish before TMEM is freed.
         commit(&sm.bar_drain);
         drain_phase(smem_u32(&sm.bar_drain), 0, a);
@@ -599,191 +520,225 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     }
     } else {
         regs_inc<kRegsSoftmax>();
-        // ------------------------------------------------------ softmax group
-        const int t = threadIdx.x;  // row inside the tile == TMEM lane
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-        const uint32_t tS = tmem + lane_base + kColS;
-        const uint32_t tO = tmem + lane_base + kColO;
-        const uint32_t tP = tmem + lane_base + kColP;
+        // ------------------------------------------------------ softmax groups
+        const int i = warp >> 2;                    // query tile of this group
+        const int t = threadIdx.x & (kBlockM - 1);  // row inside the tile == TMEM lane
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lane_base + col_s(i);
+        const uint32_t tO = tmem + lane_base + col_o(i);
+        const int n = n_kv(i);
+        const int tile_row0 = w.row0 + i * kBlockM;
+        const int row = tile_row0 + t;
+        const int shift = w.seqlen_k - w.seqlen_q;
         const float scale = a.scale;
+        // Keys visible to this row: [0, key_lim).
+        const int key_lim = kCausal ? min(w.seqlen_k, row + shift + 1) : w.seqlen_k;
+
+        float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
+        float l_run = 0.0f;       // running sum of un-normalised P
         bool ok = true;
-        int g = 0;      // flat KV step counter
-        // The tile description is parked in shared memory (one copy per warp)
-        // while the KV loop runs, so its fields hold no registers there; the
-        // loop itself needs only the scalars below.
-        TileWork* wsave = &sm.work[warp];
-        for (int k = 0; ok; ++k) {
-            const int x = work_index(a, k);
-            if (x == -1) break;
-            int n, k0, tile_lim, key_lim;
-            {
-                TileWork w;
-                if (x < 0 || !decode_work<kCausal, kVarlen>(a, x, w)) continue;
-                n = w.n;
-                k0 = w.j0 * kBlockN;
-                const int shift = w.seqlen_k - w.seqlen_q;
-                // Keys visible to this row: [0, key_lim); a KV tile needs the
-                // mask once it reaches past the smallest limit of its rows.
-                key_lim = kCausal ? min(w.seqlen_k, w.row0 + t + shift + 1) : w.seqlen_k;
-                tile_lim = kCausal ? min(w.seqlen_k, w.row0 + shift + 1) : w.seqlen_k;
-                if (lane == 0) *wsave = w;
-                __syncwarp();
+
+        const uint32_t tP = tmem + lane_base + col_p(i);
+        for (int j = 0; j < n; ++j) {
+            bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
+            uint32_t r[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) reg_fence(r[c]);
+            // S_i now lives in registers: the MMA warp may overwrite it with
+            // S_i(j+1) while this group computes P_i(j).
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sm.bar_sfree[i]));
 
-            float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
-            float l_run = 0.0f;       // running sum of un-normalised P
+            const int k0 = (w.j0 + j) * kBlockN;
+            const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
+                                   (kCausal && k0 + kBlockN - 1 > tile_row0 + shift);
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
+            }
+            // Row max: 8 independent 3-input-max chains.
+            float mx[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
+#pragma unroll
+                for (int e = 1; e < 15; e += 2)
+                    mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
+                mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
+            }
+            const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
+                                        fmaxf(mx[6], mx[7]));
+            const float m_new = fmaxf(m_run, row_max);
+            const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
+            float alpha = 1.0f;
+            if (upd) {
+                alpha = ex2_approx((m_run - m_new) * scale);
+                m_run = m_new;
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            const float neg_ms = kPLog2Bias - m_use * scale;
+            const float2 scale2 = make_float2(scale, scale);
+            const float2 neg2 = make_float2(neg_ms, neg_ms);
+            float2 sum[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
+            uint32_t p[2][32];
+            // P = exp2(S*scale - m*scale).  On tiles without masking a fixed
+            // share of the pairs (kExpPolyPairs of every 16) runs the
+            // polynomial exp2 on the FMA/ALU pipes, relieving MUFU; masked
+            // tiles (which may hold -inf) use MUFU ex2 only.
+            auto exp_tile = [&](auto poly_tag) {
+                constexpr bool kPoly = decltype(poly_tag)::value;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const int pr = e >> 1;  // pair index in the chunk
+                        const float2 x = ffma2(make_float2(__uint_as_float(r[c][e]),
+                                                           __uint_as_float(r[c][e + 1])),
+                                               scale2, neg2);
+                        float2 pp;
+                        if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
+                            pp = exp2_poly2(x);
+                        else
+                            pp = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+                        sum[pr & 3] = fadd2(sum[pr & 3], pp);
+                        p[c >> 1][(c & 1) * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
+                    }
+            };
+            if (need_mask) exp_tile(std::false_type{});
+            else exp_tile(std::true_type{});
+            const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
+            l_run = fmaf(l_run, alpha, s01.x + s01.y);
 
-            for (int j = 0; j < n; ++j, ++g) {
-                bool got = wait_phase(smem_u32(&sm.bar_s), g & 1, abort_flag, a,
-                                      kErrTimeoutSoftmax);
+            if (j > 0) {
+                // P_i(j-1) must be consumed (and O_i settled) before P_i(j) and the
+                // O_i rescale are written.
+                got = wait_phase(smem_u32(&sm.bar_pv[i]), (j - 1) & 1, abort_flag, a,
+                                 kErrTimeoutSoftmax);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                uint32_t r[4][32];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 4; ++c) reg_fence(r[c]);
-                // S now lives in registers: the MMA warp may overwrite it with
-                // S(g+1) while this group computes P(g).
-                tc_fence_before();
-                mbar_arrive(smem_u32(&sm.bar_sfree));
-
-                const bool need_mask = k0 + kBlockN > tile_lim;
-                if (need_mask) {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
-                }
-                k0 += kBlockN;
-                // Row max: 8 independent 3-input-max chains.
-                float mx[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) mx[q] = __uint_as_float(r[q >> 1][(q & 1) * 16]);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const uint32_t* rr = &r[q >> 1][(q & 1) * 16];
-#pragma unroll
-                    for (int e = 1; e < 15; e += 2)
-                        mx[q] = fmax3(mx[q], __uint_as_float(rr[e]), __uint_as_float(rr[e + 1]));
-                    mx[q] = fmaxf(mx[q], __uint_as_float(rr[15]));
-                }
-                const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]),
-                                            fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-                const float m_new = fmaxf(m_run, row_max);
-                const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
-                float alpha = 1.0f;
-                if (upd) {
-                    alpha = ex2_approx((m_run - m_new) * scale);
-                    m_run = m_new;
-                }
-                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-                const float neg_ms = kPLog2Bias - m_use * scale;
-                const float2 scale2 = make_float2(scale, scale);
-                const float2 neg2 = make_float2(neg_ms, neg_ms);
-                float2 sum[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) sum[q] = make_float2(0.0f, 0.0f);
-                uint32_t p[2][32];
-                // P = exp2(S*scale - m*scale).  On tiles without masking a
-                // fixed share of the pairs (kExpPolyPairs of every 16) runs the
-                // polynomial exp2 on the FMA/ALU pipes, relieving MUFU; masked
-                // tiles (which may hold -inf) use MUFU ex2 only.
-                auto exp_tile = [&](auto poly_tag) {
-                    constexpr bool kPoly = decltype(poly_tag)::value;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c)
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            const int pr = e >> 1;  // pair index in the chunk
-                            const float2 xx = ffma2(make_float2(__uint_as_float(r[c][e]),
-                                                                __uint_as_float(r[c][e + 1])),
-                                                    scale2, neg2);
-                            float2 pp;
-                            if (kPoly && ((pr + 1) * kExpPolyPairs / 16 > pr * kExpPolyPairs / 16))
-                                pp = exp2_poly2(xx);
-                            else
-                                pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
-                            sum[pr & 3] = fadd2(sum[pr & 3], pp);
-                            p[c >> 1][(c & 1) * 16 + pr] = pack_bf16_trunc(pp.x, pp.y);
-                        }
-                };
-                if (need_mask) exp_tile(std::false_type{});
-                else exp_tile(std::true_type{});
-                const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
-                l_run = fmaf(l_run, alpha, s01.x + s01.y);
-
-                if (g > 0) {
-                    // P(g-1) must be consumed (and O settled) before P(g) and
-                    // the O rescale are written.
-                    got = wait_phase(smem_u32(&sm.bar_pv), (g - 1) & 1, abort_flag, a,
-                                     kErrTimeoutSoftmax);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                }
-                tmem_st32(tP, p[0]);
-                tmem_st32(tP + 32, p[1]);
-                if (j > 0 && __any_sync(0xffffffffu, upd)) {
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-                        reg_fence(o);
-                        const float2 a2 = make_float2(alpha, alpha);
-#pragma unroll
-                        for (int e = 0; e < 32; e += 2) {
-                            const float2 v2 = fmul2(
-                                make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
-                            o[e] = __float_as_uint(v2.x);
-                            o[e + 1] = __float_as_uint(v2.y);
-                        }
-                        tmem_st32(tO + c * 32, o);
-                    }
-                }
-                tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive(smem_u32(&sm.bar_p));
             }
-            if (!ok) break;
-
-            // ---------------------------------------------------- epilogue
-            uint32_t o[2][32];
-            if (n == 0) {
+            tmem_st32(tP, p[0]);
+            tmem_st32(tP + 32, p[1]);
+            if (j > 0 && __any_sync(0xffffffffu, upd)) {
 #pragma unroll
-                for (int c = 0; c < 32; ++c) o[0][c] = o[1][c] = 0u;
-            } else {
-                // The tile's last P V is done: read O out, then hand the
-                // accumulator to the next tile's first P V.
-                bool got = wait_phase(smem_u32(&sm.bar_pv), (g - 1) & 1, abort_flag, a,
-                                      kErrTimeoutSoftmax);
-                if (!__all_sync(0xffffffffu, got)) {
-                    ok = false;
-                    break;
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+                    reg_fence(o);
+                    const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float2 v2 = fmul2(make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), a2);
+                        o[e] = __float_as_uint(v2.x);
+                        o[e + 1] = __float_as_uint(v2.y);
+                    }
+                    tmem_st32(tO + c * 32, o);
                 }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sm.bar_p[i]));
+        }
+
+        // ---------------------------------------------------- epilogue
+        if (ok && n > 0) {
+            bool got = wait_phase(smem_u32(&sm.bar_o[i]), 0, abort_flag, a, kErrTimeoutSoftmax);
+            ok = __all_sync(0xffffffffu, got);
+        }
+        if (ok) {
+            uint32_t o[2][32];
+            if (n > 0) {
                 tc_fence_after();
                 tmem_ld32(tO, o[0]);
                 tmem_ld32(tO + 32, o[1]);
                 tmem_wait_ld();
                 reg_fence(o[0]);
                 reg_fence(o[1]);
-                tc_fence_before();
-                mbar_arrive(smem_u32(&sm.bar_ofree));
             }
-            __syncwarp();
-            const TileWork w = *wsave;
-            __syncwarp();  // every lane has its copy before the next tile's write
-            store_row<kVarlen>(a, w, t, o, n > 0, m_run, l_run);
+            if (w.partial) {
+                // Split-KV: this item's normalised partial O (fp32) and LSE;
+                // the combine kernel merges the splits of each query block.
+                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+                const size_t prow = (size_t)blockIdx.x * kRowsPerCta + (size_t)i * kBlockM + t;
+                float4* dst = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    float v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = c * 4 + e;
+                        v[e] = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
+                    }
+                    dst[c] = make_float4(v[0], v[1], v[2], v[3]);
+                }
+                const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                a.part_lse[prow] = (l_run > 0.0f)
+                                       ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
+                                             0.69314718055994531f
+                                       : -INFINITY;
+            } else if (row < w.seqlen_q) {
+                const float inv_l = (l_run > 0.0f) ? 1.0f / l_run : 0.0f;
+                uint16_t* orow;
+                if constexpr (kVarlen) {
+                    orow = a.o + (long long)w.h * a.nhead_stride_o +
+                           (long long)(w.off_q + row) * a.stride_o;
+                } else {
+                    orow = a.o + (long long)w.b * a.batch_stride_o +
+                           (long long)w.h * a.nhead_stride_o + (long long)row * a.stride_o;
+                }
+                uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = c * 8 + e * 2;
+                        const float v0 = n > 0 ? __uint_as_float(o[col >> 5][col & 31]) * inv_l : 0.0f;
+                        const float v1 = n > 0 ? __uint_as_float(o[(col + 1) >> 5][(col + 1) & 31]) * inv_l : 0.0f;
+#ifdef FMHA_O_ROUND_TRUNC
+                        pk[e] = pack_bf16_trunc(v0, v1);  // reference kernel's rounding
+#else
+                        pk[e] = pack_bf16_rne(v0, v1);
+#endif
+                    }
+                    dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+                if (a.lse != nullptr) {
+                    const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+                    const float lse = (l_run > 0.0f)
+                                          ? (__log2f(l_run) + m_use * scale - kPLog2Bias) *
+                                                0.69314718055994531f
+                                          : -INFINITY;
+                    long long idx;
+                    if constexpr (kVarlen) {
+                        idx = (long long)w.h * a.total_q + w.off_q + row;
+                    } else {
+                        idx = ((long long)w.b * a.nhead_q + w.h) * a.seqlen_q + row;
+                    }
+                    a.lse[idx] = lse;
+                }
+            }
         }
-    }
+}
 
     // ---------------------------------------------------------- teardown
     tc_fence_before();
@@ -791,6 +746,29 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     if (warp == kWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+
+// Varlen launch order: order[r] = the sequence of rank r when sequences are
+// sorted by query length, longest first (ties by index), so the full-grid
+// varlen launch deals the heaviest query blocks out first across
+// sequences, not only inside one (src/fused/kernel.cpp:91-99 reverses the
+// block index within a sequence).  One CTA; rank by counting.
+__global__ void __launch_bounds__(1024)
+fmha_fwd_d64_varlen_order(const int32_t* __restrict__ seqstart, int batch,
+                          int32_t* __restrict__ order) {
+    extern __shared__ int32_t lens[];
+    for (int b = threadIdx.x; b < batch; b += blockDim.x) lens[b] = seqstart[b + 1] - seqstart[b];
+    __syncthreads();
+    for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+        const int lb = lens[b];
+        int rank = 0;
+        for (int c = 0; c < batch; ++c) {
+            const int lc = lens[c];
+            rank += (lc > lb) || (lc == lb && c < b);
+        }
+        order[rank] = b;
     }
 }
 
@@ -921,16 +899,21 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
 
 struct DeviceContext {
     bool ready = false;
-    int num_sms = 0;
     int* err_word = nullptr;
+    // Varlen launch-order buffers, one per stream (launches on different
+    // streams may overlap), grown on demand.
+    std::vector<std::pair<cudaStream_t, std::pair<int32_t*, int>>> orders;
 };
+
+// Largest batch the varlen ordering handles (its one CTA ranks in shared
+// memory); larger varlen launches keep the sequences' own order.
+constexpr int kOrderMaxBatch = 8192;
 
 std::mutex g_mutex;
 std::vector<DeviceContext> g_devices;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 unsigned long long g_wait_limit_ns = 2000000000ull;
 int g_stall_inject = 0;
-int g_max_ctas = 0;  // 0: kCtasPerSm per SM (persistent); < 0: one CTA per item
 
 constexpr size_t kSmemBytes = sizeof(SharedStorage) + 1024;
 
@@ -947,13 +930,12 @@ int ensure_encoder() {
     return FMHA_OK;
 }
 
-// Per device, once (device current): check it is an sm_100 part, read its SM
-// count and set the kernels' shared-memory attributes.  Allocates nothing.
-int prepare_device(int dev, int* num_sms) {
+// Per device, once (device current): check it is an sm_100 part and set the
+// kernels' shared-memory attributes.  Allocates nothing.
+int prepare_device(int dev) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return FMHA_ERR_DEVICE;
     if (prop.major != 10 || prop.minor != 0) return FMHA_ERR_DEVICE;
-    *num_sms = prop.multiProcessorCount;
     const int smem = (int)kSmemBytes;
     auto set = [smem](const void* fn) {
         cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -973,7 +955,7 @@ int ensure_context(int dev, DeviceContext** out) {
     if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1);
     DeviceContext& ctx = g_devices[dev];
     if (!ctx.ready) {
-        if ((st = prepare_device(dev, &ctx.num_sms)) != FMHA_OK) return st;
+        if ((st = prepare_device(dev)) != FMHA_OK) return st;
         if (cudaMalloc(&ctx.err_word, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
         if (cudaMemset(ctx.err_word, 0, sizeof(int)) != cudaSuccess) return FMHA_ERR_LAUNCH;
         ctx.ready = true;
@@ -1089,17 +1071,10 @@ int prepare_args(const FmhaFwdParams* p, int batch, bool varlen, int total_q, in
     return FMHA_OK;
 }
 
-// Persistent grid: at most kCtasPerSm CTAs per SM (or the caller's limit),
-// never more CTAs than work items.
-unsigned grid_for(int n_work, int num_sms) {
-    long long cap = (long long)kCtasPerSm * num_sms;
-    if (g_max_ctas > 0) cap = std::min<long long>(cap, g_max_ctas);
-    if (g_max_ctas < 0) cap = n_work;
-    return (unsigned)std::max(1ll, std::min<long long>(cap, n_work));
-}
-
-int launch_main(const KernelArgs& a, bool causal, bool varlen, unsigned grid,
-                cudaStream_t stream) {
+// One CTA per work item (query tile, or split-KV item); CTAs start in work
+// order, so the hardware hands the heaviest items out first.
+int launch_main(const KernelArgs& a, bool causal, bool varlen, int n_work, cudaStream_t stream) {
+    const unsigned grid = (unsigned)n_work;
     const dim3 block(kThreads);
     if (causal) {
         if (varlen) fmha_fwd_d64_sm100_kernel<true, true><<<grid, block, kSmemBytes, stream>>>(a);
@@ -1126,16 +1101,16 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     a.err_word = ctx->err_word;
     a.stall_inject = g_stall_inject;
 
-    a.n_work = a.m_blocks * a.num_hb;
+    int n_work = a.m_blocks * a.num_hb;
     a.tiles = tiles;
     if (tiles != nullptr) {
         if (ntiles == 0) return FMHA_OK;
-        a.n_work = ntiles;
+        n_work = ntiles;
         if (num_splits > 1) {
             a.num_splits = num_splits;
             a.part_o = workspace;
             a.part_lse = workspace + (size_t)ntiles * num_splits * kBlockM * kHeadDim;
-            a.n_work = ntiles * num_splits;
+            n_work = ntiles * num_splits;
         }
     }
     if (items != nullptr) {
@@ -1143,10 +1118,34 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
         a.items = items;
         a.part_o = workspace;
         a.part_lse = workspace + (size_t)n_items * kBlockM * kHeadDim;
-        a.n_work = n_items;
+        n_work = n_items;
     }
-    if ((st = launch_main(a, causal, varlen, grid_for(a.n_work, ctx->num_sms), stream)) !=
-        FMHA_OK)
+    if (varlen && tiles == nullptr && items == nullptr && batch > 1 && batch <= kOrderMaxBatch) {
+        int32_t* order = nullptr;
+        {
+            std::lock_guard<std::mutex> lock(g_mutex);
+            std::pair<int32_t*, int>* slot = nullptr;
+            for (auto& e : ctx->orders)
+                if (e.first == stream) slot = &e.second;
+            if (slot == nullptr) {
+                ctx->orders.push_back({stream, {nullptr, 0}});
+                slot = &ctx->orders.back().second;
+            }
+            if (slot->second < batch) {
+                if (slot->first) cudaFree(slot->first);
+                slot->first = nullptr;
+                slot->second = 0;
+                if (cudaMalloc(&slot->first, sizeof(int32_t) * (size_t)batch) != cudaSuccess)
+                    return FMHA_ERR_LAUNCH;
+                slot->second = batch;
+            }
+            order = slot->first;
+        }
+        fmha_fwd_d64_varlen_order<<<1, 1024, sizeof(int32_t) * (size_t)batch, stream>>>(
+            p->seqstart_q, batch, order);
+        a.seq_order = order;
+    }
+    if ((st = launch_main(a, causal, varlen, n_work, stream)) != FMHA_OK)
         return st;
     if (items != nullptr) {
         dim3 cgrid((unsigned)n_items, 1, 1);
@@ -1180,7 +1179,6 @@ static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocHeaderInts + 
 
 struct NoAllocDevice {
     bool ready = false;
-    int num_sms = 0;
     int32_t* scratch = nullptr;  // device address of g_noalloc_scratch on that device
 };
 std::vector<NoAllocDevice> g_noalloc;
@@ -1195,7 +1193,7 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
     if ((int)g_noalloc.size() <= dev) g_noalloc.resize(dev + 1);
     NoAllocDevice& d = g_noalloc[dev];
     if (!d.ready) {
-        if ((st = prepare_device(dev, &d.num_sms)) != FMHA_OK) return st;
+        if ((st = prepare_device(dev)) != FMHA_OK) return st;
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
             return FMHA_ERR_LAUNCH;
@@ -1212,19 +1210,20 @@ int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, 
     if (ntiles > kNoAllocMaxTiles) return FMHA_ERR_SCRATCH;
     if (ntiles > 0 && host_tiles == nullptr) return FMHA_ERR_ARG;
     const bool varlen = p->seqstart_q != nullptr;
-    KernelArgs a;
-    bool empty = false;
-    int st = prepare_args(p, batch, varlen, total_q, total_k, a, &empty);
-    if (st != FMHA_OK) return st;
     // The list is on the host, so every entry is checked before anything is
     // queued: a (batch, head) index or query block outside the problem is an
     // argument error, not a silent skip.
+    if (p->nhead_q <= 0 || p->seqlen_q < 0) return FMHA_ERR_ARG;
     const long long num_hb = (long long)p->nhead_q * batch;
     const int m_blocks = (p->seqlen_q + kBlockM - 1) / kBlockM;
     for (int i = 0; i < ntiles; ++i) {
         const int32_t hb = host_tiles[2 * i], m = host_tiles[2 * i + 1];
         if (hb < 0 || hb >= num_hb || m < 0 || m >= m_blocks) return FMHA_ERR_ARG;
     }
+    KernelArgs a;
+    bool empty = false;
+    int st = prepare_args(p, batch, varlen, total_q, total_k, a, &empty);
+    if (st != FMHA_OK) return st;
     if (ntiles == 0 || empty) return FMHA_OK;
 
     int dev = 0;
@@ -1235,7 +1234,6 @@ int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, 
     a.err_word = scratch;  // header word 0
     a.stall_inject = 0;
     a.tiles = scratch + kNoAllocHeaderInts;
-    a.n_work = ntiles;
 
     // The array keeps the previous call's contents: clear the error word and
     // stage this call's work list, in stream order before the kernel.
@@ -1244,7 +1242,7 @@ int launch_noalloc(const FmhaFwdParams* p, int batch, bool causal, int total_q, 
                         sizeof(int32_t) * 2 * (size_t)ntiles, cudaMemcpyHostToDevice,
                         stream) != cudaSuccess)
         return FMHA_ERR_LAUNCH;
-    return launch_main(a, causal, varlen, grid_for(ntiles, d->num_sms), stream);
+    return launch_main(a, causal, varlen, ntiles, stream);
 }
 
 // Reads the error word of the allocation-free scratch and clears it, so a
@@ -1372,11 +1370,6 @@ int fmha_fwd_d64_status(CUstream_st* stream) {
     return FMHA_OK;
 }
 
-void fmha_fwd_d64_set_max_ctas(int max_ctas) {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    g_max_ctas = max_ctas > 0 ? max_ctas : (max_ctas < 0 ? -1 : 0);
-}
-
 void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns) {
     std::lock_guard<std::mutex> lock(g_mutex);
     g_wait_limit_ns = limit_ns ? limit_ns : 2000000000ull;
@@ -1398,6 +1391,7 @@ void fmha_fwd_d64_release(void) {
         if (g_devices[d].ready) {
             cudaSetDevice((int)d);
             cudaFree(g_devices[d].err_word);
+            for (auto& e : g_devices[d].orders) cudaFree(e.second.first);
             g_devices[d] = DeviceContext();
         }
     }

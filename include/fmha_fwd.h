@@ -215,14 +215,6 @@ int fmha_fwd_d64_status(struct CUstream_st* stream);
  * No reference counterpart. */
 void fmha_fwd_d64_set_wait_limit_ns(unsigned long long limit_ns);
 
-/* Caps the number of persistent CTAs of subsequent launches on all devices
- * (each CTA loops over its share of the query tiles); 0 restores the default
- * of two CTAs per SM; a negative value launches one CTA per work item (no
- * persistence).  A cap leaves SMs free for work on other streams; every
- * setting computes the same results.  No reference counterpart (the reference
- * launches one work group per query tile, src/fused/kernel.cpp:55-99). */
-void fmha_fwd_d64_set_max_ctas(int max_ctas);
-
 /* Releases the per-device launcher context (error word).  No reference
  * counterpart. */
 void fmha_fwd_d64_release(void);
@@ -235,8 +227,8 @@ const char* fmha_fwd_d64_error_string(int status);
 int fmha_fwd_d64_rows_per_block(void);
 
 /* Tile geometry of the B200 kernel (informational; callers need not compute
- * launch geometry).  128 query rows per tile (persistent CTAs, two per SM,
- * loop over the tiles), 128 keys per KV tile. */
+ * launch geometry).  128 query rows per tile, one tile per CTA, two CTAs per
+ * SM, 128 keys per KV tile. */
 #define FMHA_B200_BLOCK_M 128
 #define FMHA_B200_ROWS_PER_BLOCK 128 /* query rows per work-list entry (see fmha_fwd_d64_rows_per_block) */
 #define FMHA_B200_BLOCK_N 128
