@@ -369,12 +369,13 @@ def fmha_fwd(q, k, v, causal: bool = False, return_lse: bool = False, layout: st
 def fmha_fwd_from_host(q, k, v, causal: bool = False, layout: str = "bshd", out=None,
                        chunks: int = 4, device=None):
     """O = attention(Q, K, V) for dense inputs that live in (pinned) HOST
-    memory: the batch is cut into `chunks` slices whose host->device copies,
-    kernel launches and device->host copy of O run on two streams, so the
-    PCIe transfers of one slice overlap the kernel of the previous one.
-    Returns the host tensor `out` (allocated pinned when omitted).  The
-    caller's current stream is ordered after the last copy: synchronise it
-    before reading `out`.  Device staging buffers are cached per shape."""
+    memory: the batch is cut into `chunks` slices, and three streams overlap
+    the host->device copies of slice i+1, the kernel of slice i and the
+    device->host copy of slice i-1's O (PCIe is full duplex, so the two copy
+    directions run at the same time).  Returns the host tensor `out`
+    (allocated pinned when omitted).  The caller's current stream is ordered
+    after the last copy: synchronise it before reading `out`.  Device staging
+    buffers are cached per shape and device."""
     import torch
 
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -391,34 +392,34 @@ def fmha_fwd_from_host(q, k, v, causal: bool = False, layout: str = "bshd", out=
               "dk": torch.empty(k.shape, dtype=k.dtype, device=dev),
               "dv": torch.empty(v.shape, dtype=v.dtype, device=dev),
               "do": torch.empty(q.shape, dtype=q.dtype, device=dev),
-              "copy": torch.cuda.Stream(dev), "comp": torch.cuda.Stream(dev)}
+              "h2d": torch.cuda.Stream(dev), "comp": torch.cuda.Stream(dev),
+              "d2h": torch.cuda.Stream(dev)}
         _host_state[key] = st
     cur = torch.cuda.current_stream(dev)
-    copy, comp = st["copy"], st["comp"]
-    copy.wait_stream(cur)
-    comp.wait_stream(cur)
+    h2d, comp, d2h = st["h2d"], st["comp"], st["d2h"]
+    for s_ in (h2d, comp, d2h):
+        s_.wait_stream(cur)
     bounds = [B * i // chunks for i in range(chunks + 1)]
-    done = []
     for i in range(chunks):
         b0, b1 = bounds[i], bounds[i + 1]
         if b0 == b1:
             continue
-        with torch.cuda.stream(copy):
+        with torch.cuda.stream(h2d):
             for name, h in (("dq", q), ("dk", k), ("dv", v)):
                 st[name][b0:b1].copy_(h[b0:b1], non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(copy)
-        comp.wait_event(ev)
+            loaded = torch.cuda.Event()
+            loaded.record(h2d)
+        comp.wait_event(loaded)
         fmha_fwd(st["dq"][b0:b1], st["dk"][b0:b1], st["dv"][b0:b1], causal=causal,
                  layout=layout, out=st["do"][b0:b1], stream=comp.cuda_stream)
-        ev2 = torch.cuda.Event()
-        ev2.record(comp)
-        done.append((b0, b1, ev2))
-    with torch.cuda.stream(copy):
-        for b0, b1, ev2 in done:
-            copy.wait_event(ev2)
+        done = torch.cuda.Event()
+        done.record(comp)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
             out[b0:b1].copy_(st["do"][b0:b1], non_blocking=True)
-    cur.wait_stream(copy)
+    cur.wait_stream(d2h)
+    cur.wait_stream(comp)
+    cur.wait_stream(h2d)
     return out
 
 
