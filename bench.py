@@ -246,6 +246,9 @@ def native_arm(args, workload_key):
     # the same inputs and computes its share of the query blocks.
     if world > 1 and not args.weak:
         args.shard = True
+    # --emulate-world N: one process runs rank `rank`'s share of an N-rank
+    # split (profiling a rank's kernels on one GPU); timing is per share.
+    part_world = args.emulate_world if args.emulate_world > 0 else world
     q, k, v, cu = make_inputs(w, dev, seed_base=0 if args.shard else 1000 * rank)
     tiles = None
     share = 1.0
@@ -253,21 +256,21 @@ def native_arm(args, workload_key):
     if args.shard:
         from fmha_native_b200 import shard as shd
 
-        if not w.varlen_seqs and w.batch % world == 0 and not args.items:
+        if not w.varlen_seqs and w.batch % part_world == 0 and not args.items:
             # (batch, head) partition: every rank owns a contiguous slice of
             # the batch -- its own Q/K/V/O, nothing replicated, equal work.
             shard_mode = "batch"
-            per = w.batch // world
+            per = w.batch // part_world
             sl = slice(rank * per, (rank + 1) * per)
             q, k, v = q[sl], k[sl], v[sl]
-            share = 1.0 / world
+            share = 1.0 / part_world
         else:
             # query-tile partition (few heads, long causal sequences, varlen):
             # LPT over all query blocks, K/V replicated on every rank.
             shard_mode = "tiles"
             blocks = shd.plan_blocks(w.batch, w.heads, w.seqlen, w.seqlen, w.causal,
                                      w.varlen_seqs)
-            part = shd.partition(blocks, world)[rank]
+            part = shd.partition(blocks, part_world)[rank]
             tiles = torch.from_numpy(shd.tiles_array(part)).to(dev)
             share = sum(b[2] for b in part) / sum(b[2] for b in blocks)
     splits = 1
@@ -356,6 +359,17 @@ def native_arm(args, workload_key):
     value = flops_job / (ms_step * 1e-3) / 1e12
     peak_tf, peak_hbm, peak_kind = load_peaks()
     achieved = flops_rank / (statistics.mean(kern_ms) * 1e-3) / 1e12
+
+    if args.launch_only:
+        if rank == 0:
+            print(json.dumps({"launch_only": True, "workload": w.name,
+                              "share_tflops": round(achieved, 2), "share": round(share, 4),
+                              "unit": UNIT, "ms_per_step": round(ms_step, 5), "splits": splits,
+                              "items": int(items.shape[0]) if items is not None else 0}),
+                  flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
 
     # ---- e2e: host buffers through the public API, copies inside the timed region
     e2e = e2e_measure(fm, w, dev, args, tiles, splits, items,
@@ -594,6 +608,10 @@ def main():
                     help="N>1: every rank runs its own copy of the workload (weak scaling)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch to report in roofline.traffic")
+    ap.add_argument("--launch-only", action="store_true",
+                    help="time the kernel launches only (no e2e, no CPU leg): profiling runs")
+    ap.add_argument("--emulate-world", type=int, default=0,
+                    help="with --shard on one process: run rank 0's share of an N-rank split")
     ap.add_argument("--sweep", action="store_true",
                     help="the reference's 8-config sweep (+ varlen) on the bench_fmha_fwd CLI")
     ap.add_argument("--mask", type=int, default=0, help="--sweep: causal mask 0|1")

@@ -57,6 +57,8 @@ WORKLOADS = {
                     layout="thd", varlen_seqs=tuple(varlen_lengths())),
     "c5a": Workload("B1 H2 S40000 D64 bf16 causal +LSE", 1, 2, 40000, True, True),
     "c5b": Workload("B32 H32 S4096 D64 bf16 causal", 32, 32, 4096, True, False),
+    # one eighth of c5b (its per-rank share at 8 GPUs): the profiling case
+    "c5b_s8": Workload("B4 H32 S4096 D64 bf16 causal (c5b / 8)", 4, 32, 4096, True, False),
 }
 
 
