@@ -772,14 +772,21 @@ fmha_fwd_d64_varlen_order(const int32_t* __restrict__ seqstart, int batch,
     }
 }
 
-// Split-KV merge of one query row: partial slots [slot0, slot0 + nparts) of
-// query block mblk of (batch, head) hb; LSE = log(sum_s exp(lse_s)),
-// O = sum_s exp(lse_s - LSE) * O_s, rounded to bf16 like the main epilogue;
-// the same LSE merge the reference's base-2 epilogue formula implies
-// (src/fused/op_epilog.hpp:92-98).
+// Split-KV merge: partial slots [slot0, slot0 + nparts) of query block mblk
+// of (batch, head) hb -> O (bf16, rounded like the main epilogue) and LSE:
+// LSE = log(sum_s exp(lse_s)), O = sum_s exp(lse_s - LSE) * O_s -- the LSE
+// merge the reference's base-2 epilogue formula implies
+// (src/fused/op_epilog.hpp:92-98).  A CTA of kCombineThreads merges
+// kCombineRows rows of the block (quarter `part`): 16 threads per row, each
+// owning 4 of the 64 columns, so a partial row is one coalesced 256-byte
+// read and the splits' loads are independent.
+constexpr int kCombineThreads = 512;
+constexpr int kCombineRows = kCombineThreads / 16;          // 32 rows per CTA
+constexpr int kCombineParts = kBlockM / kCombineRows;       // 4 CTAs per block
+
 template <bool kVarlen>
-__device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk, int slot0,
-                                          int nparts, int r) {
+__device__ __forceinline__ void merge_rows(const KernelArgs& a, int hb, int mblk, int slot0,
+                                           int nparts, int part) {
     // Malformed list entries are skipped before any address is formed.
     if (hb < 0 || hb >= a.num_hb || mblk < 0 || mblk >= a.m_blocks) return;
     const int h = hb % a.nhead_q, b = hb / a.nhead_q;
@@ -789,14 +796,14 @@ __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk,
         seqlen_q = a.seqstart_q[b + 1] - off_q;
         if (off_q < 0 || seqlen_q < 0 || off_q + seqlen_q > a.total_q) return;
     }
+    const int r = part * kCombineRows + (int)(threadIdx.x >> 4);  // row inside the block
+    const int c4 = threadIdx.x & 15;                              // float4 column group
     const int row = mblk * kBlockM + r;
     if (row >= seqlen_q) return;
     float mx = -INFINITY;
     for (int s = 0; s < nparts; ++s)
         mx = fmaxf(mx, a.part_lse[(size_t)(slot0 + s) * kBlockM + r]);
-    float acc[kHeadDim];
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) acc[d] = 0.0f;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float wsum = 0.0f;
     if (mx != -INFINITY) {
         for (int s = 0; s < nparts; ++s) {
@@ -805,15 +812,11 @@ __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk,
             if (l == -INFINITY) continue;
             const float wgt = __expf(l - mx);
             wsum += wgt;
-            const float4* src = reinterpret_cast<const float4*>(a.part_o + prow * kHeadDim);
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const float4 v = src[c];
-                acc[4 * c] += wgt * v.x;
-                acc[4 * c + 1] += wgt * v.y;
-                acc[4 * c + 2] += wgt * v.z;
-                acc[4 * c + 3] += wgt * v.w;
-            }
+            const float4 v = reinterpret_cast<const float4*>(a.part_o + prow * kHeadDim)[c4];
+            acc.x += wgt * v.x;
+            acc.y += wgt * v.y;
+            acc.z += wgt * v.z;
+            acc.w += wgt * v.w;
         }
     }
     const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
@@ -824,21 +827,15 @@ __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk,
         orow = a.o + (long long)b * a.batch_stride_o + (long long)h * a.nhead_stride_o +
                (long long)row * a.stride_o;
     }
-    uint4* dst = reinterpret_cast<uint4*>(orow);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
 #ifdef FMHA_O_ROUND_TRUNC
-            pk[e] = pack_bf16_trunc(acc[c * 8 + 2 * e] * inv, acc[c * 8 + 2 * e + 1] * inv);
+    const uint2 pk = make_uint2(pack_bf16_trunc(acc.x * inv, acc.y * inv),
+                                pack_bf16_trunc(acc.z * inv, acc.w * inv));
 #else
-            pk[e] = pack_bf16_rne(acc[c * 8 + 2 * e] * inv, acc[c * 8 + 2 * e + 1] * inv);
+    const uint2 pk = make_uint2(pack_bf16_rne(acc.x * inv, acc.y * inv),
+                                pack_bf16_rne(acc.z * inv, acc.w * inv));
 #endif
-        }
-        dst[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-    if (a.lse != nullptr) {
+    reinterpret_cast<uint2*>(orow)[c4] = pk;
+    if (a.lse != nullptr && c4 == 0) {
         const float lse = wsum > 0.0f ? mx + __logf(wsum) : -INFINITY;
         const long long idx = kVarlen ? (long long)h * a.total_q + off_q + row
                                       : ((long long)b * a.nhead_q + h) * a.seqlen_q + row;
@@ -846,25 +843,26 @@ __device__ __forceinline__ void merge_row(const KernelArgs& a, int hb, int mblk,
     }
 }
 
-// Uniform split-KV combine: block g merges slots [g*S, g*S + S) of tiles[g].
+// Uniform split-KV combine: CTA (g, part) merges slots [g*S, g*S + S) of
+// tiles[g], rows of quarter `part`.
 template <bool kVarlen>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kCombineThreads)
 fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
-    const int item_block = blockIdx.x;
+    const int item_block = blockIdx.x / kCombineParts;
     if (item_block >= nblocks) return;
-    merge_row<kVarlen>(a, a.tiles[2 * item_block], a.tiles[2 * item_block + 1],
-                       item_block * a.num_splits, a.num_splits, threadIdx.x);
+    merge_rows<kVarlen>(a, a.tiles[2 * item_block], a.tiles[2 * item_block + 1],
+                        item_block * a.num_splits, a.num_splits, blockIdx.x % kCombineParts);
 }
 
-// Work-item combine: block x merges the run of consecutive partial items of
-// one query block that starts at item x (other blocks return at once).  The
-// run length is found with one parallel probe per thread (128 items per
-// pass), not a chain of dependent loads.
+// Work-item combine: CTA (x, part) merges the run of consecutive partial
+// items of one query block that starts at item x (CTAs of other items return
+// at once).  The run length is found with one parallel probe per thread
+// (kCombineThreads items per pass), not a chain of dependent loads.
 template <bool kVarlen>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kCombineThreads)
 fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
     __shared__ int run_end;
-    const int x = blockIdx.x;
+    const int x = blockIdx.x / kCombineParts;
     const int4* items = reinterpret_cast<const int4*>(a.items);
     // A partial item has a well-formed KV range; malformed items were skipped
     // by the main kernel (no partial result) and take no part in any run.
@@ -876,7 +874,7 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
         if (partial(prev) && prev.x == it.x && prev.y == it.y) return;  // not the run's head
     }
     int n = 0;
-    for (int base = x + 1;; base += 128) {
+    for (int base = x + 1;; base += kCombineThreads) {
         if (threadIdx.x == 0) run_end = n_items;
         __syncthreads();
         const int y = base + (int)threadIdx.x;
@@ -887,12 +885,12 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
         __syncthreads();
         const int e = run_end;
         __syncthreads();
-        if (e < base + 128 || base + 128 >= n_items) {
+        if (e < base + kCombineThreads || base + kCombineThreads >= n_items) {
             n = min(e, n_items) - x;
             break;
         }
     }
-    merge_row<kVarlen>(a, it.x, it.y, x, n, threadIdx.x);
+    merge_rows<kVarlen>(a, it.x, it.y, x, n, blockIdx.x % kCombineParts);
 }
 
 // ====================================================================== host
@@ -1148,13 +1146,13 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     if ((st = launch_main(a, causal, varlen, n_work, stream)) != FMHA_OK)
         return st;
     if (items != nullptr) {
-        dim3 cgrid((unsigned)n_items, 1, 1);
-        if (varlen) fmha_fwd_d64_items_combine<true><<<cgrid, 128, 0, stream>>>(a, n_items);
-        else fmha_fwd_d64_items_combine<false><<<cgrid, 128, 0, stream>>>(a, n_items);
+        dim3 cgrid((unsigned)(n_items * kCombineParts), 1, 1);
+        if (varlen) fmha_fwd_d64_items_combine<true><<<cgrid, kCombineThreads, 0, stream>>>(a, n_items);
+        else fmha_fwd_d64_items_combine<false><<<cgrid, kCombineThreads, 0, stream>>>(a, n_items);
     } else if (a.num_splits > 1) {
-        dim3 cgrid((unsigned)ntiles, 1, 1);
-        if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, 128, 0, stream>>>(a, ntiles);
-        else fmha_fwd_d64_splitkv_combine<false><<<cgrid, 128, 0, stream>>>(a, ntiles);
+        dim3 cgrid((unsigned)(ntiles * kCombineParts), 1, 1);
+        if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, kCombineThreads, 0, stream>>>(a, ntiles);
+        else fmha_fwd_d64_splitkv_combine<false><<<cgrid, kCombineThreads, 0, stream>>>(a, ntiles);
     }
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
 }
