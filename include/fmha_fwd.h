@@ -184,10 +184,8 @@ int fmha_fwd_d64_bf16_items(const FmhaFwdParams* params, int batch, int causal,
  *                copied with cudaMemcpyAsync on `stream`.  From pageable
  *                memory the copy is staged before the call returns, so the
  *                array may be reused at once; from pinned (page-locked)
- *                memory the GPU reads it later, in stream order, so it must
- *                stay unchanged until the stream has passed the call -- and,
- *                if the call is captured into a CUDA graph, for as long as
- *                the graph is replayed (each replay reads it again).
+ *                memory the GPU reads it when the copy executes, so it must
+ *                stay unchanged until the stream has executed the call.
  *   ntiles     : at most 16384, else FMHA_ERR_SCRATCH and nothing is launched.
  * The first call on a device resolves the scratch address for that device
  * (make it before any stream capture begins).  All calls share the one array
