@@ -157,8 +157,10 @@ struct alignas(1024) SharedStorage {
     uint64_t bar_pv[kTilesPerCta];     // O_i += P_i V done (MMA commit)
     uint64_t bar_o[kTilesPerCta];
     uint64_t bar_drain;
+    uint64_t bar_dec;                  // softmax's verdict on the first pass (128 arrivals)
     uint32_t tmem_base;
     int abort_flag;
+    int rerun;                         // a row's scores outgrew the fixed reference: exact pass
 };
 
 // Bounded wait on an mbarrier phase.  Returns false if the CTA-wide abort
@@ -337,7 +339,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             mbar_init(smem_u32(&sm.bar_empty[s]), 1);
         }
         mbar_init(smem_u32(&sm.bar_drain), 1);
+        mbar_init(smem_u32(&sm.bar_dec), 32 * kSoftmaxWarps);
         sm.abort_flag = 0;
+        sm.rerun = 0;
         fence_barrier_init();
     }
     if (warp == kWarpMma) {
@@ -377,7 +381,17 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             int issued = 0;  // loads issued into the ring
             bool ok = true;
             const int n_loads = 2 * n_max;
-            for (int idx = 0; idx < n_loads; ++idx) {
+            // Pass 1 (the exact rerun, rare) streams the same K/V tiles again.
+            for (int pass = 0; pass < 2 && ok && n_loads > 0; ++pass) {
+            if (pass == 1) {
+                if (!wait_phase(smem_u32(&sm.bar_dec), 0, abort_flag, a, kErrTimeoutLoad)) {
+                    ok = false;
+                    break;
+                }
+                if (!*reinterpret_cast<volatile int*>(&sm.rerun)) break;
+            }
+            for (int li = 0; li < n_loads; ++li) {
+                const int idx = pass * n_loads + li;
                 const int slot = idx % kStages;
                 const uint32_t use = idx / kStages;
                 if (!wait_phase(smem_u32(&sm.bar_empty[slot]), (use & 1) ^ 1, abort_flag, a,
@@ -392,11 +406,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
                 const uint32_t bar = smem_u32(&sm.bar_full[slot]);
                 mbar_arrive_expect_tx(bar, kTileBytes);
-                const CUtensorMap* tm = (idx & 1) ? &a.tm_v : &a.tm_k;
+                const CUtensorMap* tm = (li & 1) ? &a.tm_v : &a.tm_k;
                 tma_load_rows<kVarlen>(smem_u32(sm.kv[slot]), tm, bar,
-                                       w.off_k + (w.j0 + (idx >> 1)) * kBlockN, w.kvh,
+                                       w.off_k + (w.j0 + (li >> 1)) * kBlockN, w.kvh,
                                        kVarlen ? 0 : w.b, pol_kv);
                 issued = idx + 1;
+            }
             }
             if (!ok || *abort_flag) {
                 // Let every copy this warp started land before the CTA exits.
@@ -465,24 +480,34 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 
         for (int i = 0; i < kTilesPerCta && ok; ++i)
             if (n_kv(i) > 0) ok = wait_all(&sm.bar_q[i], 0);
-        if (ok && n_max > 0) {
-            ok = wait_all(&sm.bar_full[slot_of(0)], full_parity(0));
-            if (ok) {
-                tc_fence_after();
-                for (int i = 0; i < kTilesPerCta; ++i) {
-                    if (n_kv(i) == 0) continue;
-                    issue_s(i, slot_of(0));
-                    commit(&sm.bar_s[i]);
-                }
-                commit(&sm.bar_empty[slot_of(0)]);
+        // Pass 0 is the whole schedule; pass 1 (the exact rerun) repeats it
+        // when the softmax asks for it, flat step index G + j.
+        for (int pass = 0; pass < 2 && ok && n_max > 0; ++pass) {
+        const int G = pass * n_max;
+        if (pass == 1) {
+            ok = wait_all(&sm.bar_dec, 0);
+            if (!ok || !*reinterpret_cast<volatile int*>(&sm.rerun)) break;
+            // S(G) overwrites S(G-1): the softmax has read it.
+            ok = wait_all(&sm.bar_sfree[0], (G - 1) & 1);
+            if (!ok) break;
+        }
+        ok = wait_all(&sm.bar_full[slot_of(2 * G)], full_parity(2 * G));
+        if (ok) {
+            tc_fence_after();
+            for (int i = 0; i < kTilesPerCta; ++i) {
+                if (n_kv(i) == 0) continue;
+                issue_s(i, slot_of(2 * G));
+                commit(&sm.bar_s[i]);
             }
+            commit(&sm.bar_empty[slot_of(2 * G)]);
         }
         // Steady state, per KV tile j:
         //   S_i(j+1) as soon as softmax i has read S_i(j) (s_free) and K_{j+1}
         //   landed, then O_i += P_i(j) V_j once P_i(j) is written (p_full).
         for (int j = 0; j < n_max && ok; ++j) {
-            const int v_idx = 2 * j + 1;
-            const int k_idx = 2 * j + 2;
+            const int g = G + j;
+            const int v_idx = 2 * g + 1;
+            const int k_idx = 2 * g + 2;
             bool k_used = false;
             for (int i = 0; i < kTilesPerCta; ++i) {
                 if (j + 1 >= n_kv(i)) continue;
@@ -491,7 +516,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     if (!ok) break;
                     k_used = true;
                 }
-                ok = wait_all(&sm.bar_sfree[i], j & 1);
+                ok = wait_all(&sm.bar_sfree[i], g & 1);
                 if (!ok) break;
                 tc_fence_after();
                 issue_s(i, slot_of(k_idx));
@@ -503,7 +528,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             if (!ok) break;
             for (int i = 0; i < kTilesPerCta; ++i) {
                 if (j >= n_kv(i)) continue;
-                ok = wait_all(&sm.bar_p[i], j & 1);
+                ok = wait_all(&sm.bar_p[i], g & 1);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(i, slot_of(v_idx), j > 0);
@@ -512,6 +537,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             }
             if (!ok) break;
             commit(&sm.bar_empty[slot_of(v_idx)]);
+        }
         }
         // All MMAs this warp issued must finish before TMEM is freed.
         commit(&sm.bar_drain);
@@ -537,10 +563,30 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         float m_run = -INFINITY;  // un-scaled running max used as exp2 reference
         float l_run = 0.0f;       // running sum of un-normalised P
         bool ok = true;
+        // Pass 0 ("fixed reference"): the exact row max of the first KV tile is
+        // the exp2 reference for every later tile, so later tiles skip the row
+        // max.  Any reference works as long as no P overflows: a later tile
+        // whose row sum exceeds 2^40 (scores more than 40 log2 units above the
+        // first tile's maximum) or a row with no visible key in the first tile
+        // but some later flags the CTA, and pass 1 recomputes the query tile
+        // with the exact running max (lazy rescale) -- rare, correct for any
+        // input.
+        int pass = 0;
+        const int key_end0 = (w.j0 + 1) * kBlockN;  // keys of the first KV tile: [.., key_end0)
 
         const uint32_t tP = tmem + lane_base + col_p(i);
+        // One pass over the KV tiles; kFixed selects the fixed-reference
+        // variant at compile time, so each pass runs its own straight loop.
+        // Returns whether a row outgrew the fixed reference.
+        auto kv_pass = [&](auto fixed_tag) -> bool {
+        constexpr bool fixed_ref = decltype(fixed_tag)::value;
+        const int G = fixed_ref ? 0 : n;
+        bool outgrown = false;
+        m_run = -INFINITY;
+        l_run = 0.0f;
         for (int j = 0; j < n; ++j) {
-            bool got = wait_phase(smem_u32(&sm.bar_s[i]), j & 1, abort_flag, a, kErrTimeoutSoftmax);
+            const int g = G + j;
+            bool got = wait_phase(smem_u32(&sm.bar_s[i]), g & 1, abort_flag, a, kErrTimeoutSoftmax);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
                 break;
@@ -567,6 +613,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                     for (int e = 0; e < 32; ++e)
                         if (k0 + c * 32 + e >= key_lim) r[c][e] = __float_as_uint(-INFINITY);
             }
+            bool upd = false;
+            float alpha = 1.0f;
+            if (!fixed_ref || j == 0) {
             // Row max: 8 independent 3-input-max chains.
             float mx[8];
 #pragma unroll
@@ -582,11 +631,12 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             const float row_max = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]),
                                         fmaxf(mx[6], mx[7]));
             const float m_new = fmaxf(m_run, row_max);
-            const bool upd = (m_new - m_run) * scale > kRescaleThreshold;
-            float alpha = 1.0f;
+            upd = (m_new - m_run) * scale > kRescaleThreshold;
             if (upd) {
                 alpha = ex2_approx((m_run - m_new) * scale);
                 m_run = m_new;
+            }
+            if (fixed_ref && m_run == -INFINITY && key_lim > key_end0) outgrown = true;
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             const float neg_ms = kPLog2Bias - m_use * scale;
@@ -622,12 +672,14 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             if (need_mask) exp_tile(std::false_type{});
             else exp_tile(std::true_type{});
             const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
-            l_run = fmaf(l_run, alpha, s01.x + s01.y);
+            const float tsum = s01.x + s01.y;
+            l_run = fmaf(l_run, alpha, tsum);
+            if (fixed_ref && !(tsum <= 0x1p40f)) outgrown = true;  // also catches inf / NaN
 
-            if (j > 0) {
-                // P_i(j-1) must be consumed (and O_i settled) before P_i(j) and the
+            if (g > 0) {
+                // P_i(g-1) must be consumed (and O_i settled) before P_i(g) and the
                 // O_i rescale are written.
-                got = wait_phase(smem_u32(&sm.bar_pv[i]), (j - 1) & 1, abort_flag, a,
+                got = wait_phase(smem_u32(&sm.bar_pv[i]), (g - 1) & 1, abort_flag, a,
                                  kErrTimeoutSoftmax);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
@@ -658,10 +710,26 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_p[i]));
         }
+        return outgrown;
+        };
+        const bool outgrown = kv_pass(std::true_type{});
+        if (ok && n > 0) {
+            // Verdict on pass 0, shared with the producer and MMA warps.
+            if (__any_sync(0xffffffffu, outgrown) && lane == 0) atomicOr(&sm.rerun, 1);
+            mbar_arrive(smem_u32(&sm.bar_dec));
+            const bool got = wait_phase(smem_u32(&sm.bar_dec), 0, abort_flag, a, kErrTimeoutSoftmax);
+            if (!__all_sync(0xffffffffu, got)) {
+                ok = false;
+            } else if (*reinterpret_cast<volatile int*>(&sm.rerun)) {
+                pass = 1;
+                kv_pass(std::false_type{});
+            }
+        }
 
         // ---------------------------------------------------- epilogue
         if (ok && n > 0) {
-            bool got = wait_phase(smem_u32(&sm.bar_o[i]), 0, abort_flag, a, kErrTimeoutSoftmax);
+            bool got = wait_phase(smem_u32(&sm.bar_o[i]), pass & 1, abort_flag, a,
+                                  kErrTimeoutSoftmax);
             ok = __all_sync(0xffffffffu, got);
         }
         if (ok) {

@@ -1,6 +1,9 @@
 """Score distributions that stress the online softmax's reference-max
 handling: a row max that rises tile after tile, isolated key spikes whose
-jump exceeds 2^64 in P units, and a max found in the first tile only.
+jump exceeds 2^64 in P units, a max found in the first tile only, and a late
+jump far above the first KV tile's maximum (which makes the kernel's first
+pass -- exp2 reference fixed at the first tile's maximum -- hand the query
+tile to its exact second pass).
 
 The reference's kernel keeps an exact running max
 (src/fused/op_softmax.hpp:12, softmax_row_max at :148); this kernel moves its
@@ -45,6 +48,14 @@ def _inputs(kind: str, seed: int):
     elif kind == "falling":
         q += common
         k[:, 5] = 8.0 * common
+    elif kind == "late_jump":
+        # The first 128 keys carry small scores; one key in the middle of the
+        # sequence scores ~60 log2 units (~330 raw) above them: the kernel's
+        # first pass (reference fixed at the first KV tile's maximum) flags
+        # the rows and the exact pass recomputes the tile.
+        q += common
+        k[:, :128] *= 0.05
+        k[:, 600] = 6.0 * common
     else:
         raise ValueError(kind)
     bits = [O.f32_to_bf16_bits_trunc(x.ravel()) for x in (q, k, v)]
@@ -52,7 +63,7 @@ def _inputs(kind: str, seed: int):
 
 
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("kind", ["rising", "spikes", "falling"])
+@pytest.mark.parametrize("kind", ["rising", "spikes", "falling", "late_jump"])
 def test_reference_max_moves(cuda_device, kind, causal):
     import torch
 
