@@ -584,12 +584,16 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         bool outgrown = false;
         m_run = -INFINITY;
         l_run = 0.0f;
-        for (int j = 0; j < n; ++j) {
+        // One KV step; the first step of a pass is compiled separately
+        // (kFirst), so the fixed-reference loop over the later steps carries
+        // no row-max code at all.
+        auto step = [&](int j, auto first_tag) -> bool {
+            constexpr bool first = decltype(first_tag)::value;
             const int g = G + j;
             bool got = wait_phase(smem_u32(&sm.bar_s[i]), g & 1, abort_flag, a, kErrTimeoutSoftmax);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
-                break;
+                return false;
             }
             tc_fence_after();
             uint32_t r[4][32];
@@ -615,7 +619,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             }
             bool upd = false;
             float alpha = 1.0f;
-            if (!fixed_ref || j == 0) {
+            if (!fixed_ref || first) {
             // Row max: 8 independent 3-input-max chains.
             float mx[8];
 #pragma unroll
@@ -683,7 +687,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                                  kErrTimeoutSoftmax);
                 if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
-                    break;
+                    return false;
                 }
                 tc_fence_after();
             }
@@ -709,6 +713,11 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_p[i]));
+                    return true;
+        };
+        if (n > 0 && step(0, std::true_type{})) {
+            for (int j = 1; j < n; ++j)
+                if (!step(j, std::false_type{})) break;
         }
         return outgrown;
         };
