@@ -27,6 +27,12 @@
 // proves every earlier MMA finished, which is what makes the softmax-side O
 // rescale race free.
 //
+// The exp2 reference m: the first pass takes the exact row max of the first
+// KV tile and keeps it for every later tile (no row max there); a tile whose
+// row sum of P exceeds 2^40 means the reference was outgrown, and the CTA
+// then runs a second, exact pass (running max, lazy rescale) over the same
+// tiles, continuing every barrier phase on a flat step index.
+//
 // CTAs start in work order (heaviest query tiles first inside L2-sized head
 // groups), so the hardware block scheduler balances the load dynamically.  A
 // persistent variant (two resident CTAs per SM looping over the tiles, Q
