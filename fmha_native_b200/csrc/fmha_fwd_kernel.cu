@@ -581,7 +581,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         const int key_end0 = (w.j0 + 1) * kBlockN;  // keys of the first KV tile: [.., key_end0)
 
         const uint32_t tP = tmem + lane_base + col_p(i);
-        // One pass over the KV tiles; kFixed selects the fixed-reference
+        // One pass over the KV tiles; fixed_tag selects the fixed-reference
         // variant at compile time, so each pass runs its own straight loop.
         // Returns whether a row outgrew the fixed reference.
         auto kv_pass = [&](auto fixed_tag) -> bool {
@@ -591,7 +591,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         m_run = -INFINITY;
         l_run = 0.0f;
         // One KV step; the first step of a pass is compiled separately
-        // (kFirst), so the fixed-reference loop over the later steps carries
+        // (first_tag), so the fixed-reference loop over the later steps carries
         // no row-max code at all.
         auto step = [&](int j, auto first_tag) -> bool {
             constexpr bool first = decltype(first_tag)::value;
