@@ -742,6 +742,9 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         }
 
         // ---------------------------------------------------- epilogue
+        // The merge launched after a split launch may be scheduled now: it
+        // waits on the GPU for this grid to finish before reading anything.
+        griddep_launch_dependents();
         if (ok && n > 0) {
             bool got = wait_phase(smem_u32(&sm.bar_o[i]), pass & 1, abort_flag, a,
                                   kErrTimeoutSoftmax);
@@ -883,24 +886,48 @@ __device__ __forceinline__ void merge_rows(const KernelArgs& a, int hb, int mblk
     const int c4 = threadIdx.x & 15;                              // float4 column group
     const int row = mblk * kBlockM + r;
     if (row >= seqlen_q) return;
+    // Online merge in batches of kMergeBatch splits: the batch's LSEs and
+    // partial rows are loaded together (independent loads in flight), then
+    // folded into the running maximum / weight sum / accumulator.
+    constexpr int kMergeBatch = 8;
     float mx = -INFINITY;
-    for (int s = 0; s < nparts; ++s)
-        mx = fmaxf(mx, a.part_lse[(size_t)(slot0 + s) * kBlockM + r]);
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float wsum = 0.0f;
-    if (mx != -INFINITY) {
-        for (int s = 0; s < nparts; ++s) {
-            const size_t prow = (size_t)(slot0 + s) * kBlockM + r;
-            const float l = a.part_lse[prow];
-            if (l == -INFINITY) continue;
-            const float wgt = __expf(l - mx);
-            wsum += wgt;
-            const float4 v = reinterpret_cast<const float4*>(a.part_o + prow * kHeadDim)[c4];
-            acc.x += wgt * v.x;
-            acc.y += wgt * v.y;
-            acc.z += wgt * v.z;
-            acc.w += wgt * v.w;
+    for (int s0 = 0; s0 < nparts; s0 += kMergeBatch) {
+        float l[kMergeBatch];
+        float4 v[kMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+            if (s0 + u < nparts) {
+                const size_t prow = (size_t)(slot0 + s0 + u) * kBlockM + r;
+                l[u] = a.part_lse[prow];
+                v[u] = reinterpret_cast<const float4*>(a.part_o + prow * kHeadDim)[c4];
+            } else {
+                l[u] = -INFINITY;
+                v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
         }
+        float mb = l[0];
+#pragma unroll
+        for (int u = 1; u < kMergeBatch; ++u) mb = fmaxf(mb, l[u]);
+        const float mn = fmaxf(mx, mb);
+        if (mn == -INFINITY) continue;  // no visible key in any split so far
+        const float sc = __expf(mx - mn);  // 0 while mx is still -inf
+        acc.x *= sc;
+        acc.y *= sc;
+        acc.z *= sc;
+        acc.w *= sc;
+        wsum *= sc;
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const float wgt = l[u] == -INFINITY ? 0.0f : __expf(l[u] - mn);
+            wsum += wgt;
+            acc.x += wgt * v[u].x;
+            acc.y += wgt * v[u].y;
+            acc.z += wgt * v[u].z;
+            acc.w += wgt * v[u].w;
+        }
+        mx = mn;
     }
     const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
     uint16_t* orow;
@@ -931,6 +958,7 @@ __device__ __forceinline__ void merge_rows(const KernelArgs& a, int hb, int mblk
 template <bool kVarlen>
 __global__ void __launch_bounds__(kCombineThreads)
 fmha_fwd_d64_splitkv_combine(const __grid_constant__ KernelArgs a, int nblocks) {
+    griddep_wait();  // the split launch has finished and its partials are visible
     const int item_block = blockIdx.x / kCombineParts;
     if (item_block >= nblocks) return;
     merge_rows<kVarlen>(a, a.tiles[2 * item_block], a.tiles[2 * item_block + 1],
@@ -945,6 +973,7 @@ template <bool kVarlen>
 __global__ void __launch_bounds__(kCombineThreads)
 fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
     __shared__ int run_end;
+    griddep_wait();  // the split launch has finished and its partials are visible
     const int x = blockIdx.x / kCombineParts;
     const int4* items = reinterpret_cast<const int4*>(a.items);
     // A partial item has a well-formed KV range; malformed items were skipped
@@ -977,6 +1006,23 @@ fmha_fwd_d64_items_combine(const __grid_constant__ KernelArgs a, int n_items) {
 }
 
 // ====================================================================== host
+
+// Launch a merge kernel (KernelArgs, count) of kCombineThreads threads as a
+// programmatic dependent of the previous launch on `stream`.
+cudaError_t launch_dependent(void (*kern)(KernelArgs, int), dim3 grid, cudaStream_t stream,
+                             const KernelArgs& a, int n) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kCombineThreads, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a, n);
+}
 
 struct DeviceContext {
     bool ready = false;
@@ -1228,14 +1274,20 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
     }
     if ((st = launch_main(a, causal, varlen, n_work, stream)) != FMHA_OK)
         return st;
+    // The merge goes out with programmatic stream serialization, so its
+    // launch overlaps the split launch's tail (see griddep_wait).
     if (items != nullptr) {
-        dim3 cgrid((unsigned)(n_items * kCombineParts), 1, 1);
-        if (varlen) fmha_fwd_d64_items_combine<true><<<cgrid, kCombineThreads, 0, stream>>>(a, n_items);
-        else fmha_fwd_d64_items_combine<false><<<cgrid, kCombineThreads, 0, stream>>>(a, n_items);
+        const dim3 cgrid((unsigned)(n_items * kCombineParts), 1, 1);
+        if (launch_dependent(varlen ? fmha_fwd_d64_items_combine<true>
+                                    : fmha_fwd_d64_items_combine<false>,
+                             cgrid, stream, a, n_items) != cudaSuccess)
+            return FMHA_ERR_LAUNCH;
     } else if (a.num_splits > 1) {
-        dim3 cgrid((unsigned)(ntiles * kCombineParts), 1, 1);
-        if (varlen) fmha_fwd_d64_splitkv_combine<true><<<cgrid, kCombineThreads, 0, stream>>>(a, ntiles);
-        else fmha_fwd_d64_splitkv_combine<false><<<cgrid, kCombineThreads, 0, stream>>>(a, ntiles);
+        const dim3 cgrid((unsigned)(ntiles * kCombineParts), 1, 1);
+        if (launch_dependent(varlen ? fmha_fwd_d64_splitkv_combine<true>
+                                    : fmha_fwd_d64_splitkv_combine<false>,
+                             cgrid, stream, a, ntiles) != cudaSuccess)
+            return FMHA_ERR_LAUNCH;
     }
     return cudaGetLastError() == cudaSuccess ? FMHA_OK : FMHA_ERR_LAUNCH;
 }

@@ -39,6 +39,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+// Programmatic dependent launch: a grid launched after this one with
+// programmatic stream serialization may start once every CTA of this grid
+// has signalled (or exited); it then waits in griddep_wait() until this
+// grid has completed and its memory is visible.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // One elected lane of a converged warp (the same lane on every call while
 // the warp stays converged).
 __device__ __forceinline__ bool elect_one() {

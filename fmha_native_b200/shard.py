@@ -102,32 +102,39 @@ def tiles_array(part: Sequence[Block]):
 Item = Tuple[int, int, int, int]  # (b*nhead_q + h, query block, kv_begin, kv_end)
 
 
-def plan_items(part: Sequence[Block], slots: int = 2 * 148,
+def plan_items(part: Sequence[Block], slots: int = 2 * 148, waves: float = 1.0,
                min_chunk: int = 4) -> List[Item]:
-    """Work items for fmha_fwd_d64_bf16_items: a block whose KV range is
-    longer than `chunk` tiles is cut into near-equal consecutive ranges
-    (partial items, merged after the launch); the others stay whole
-    (kv_end = -1, written directly).  Splitting starts only when the
-    heaviest block exceeds the average load of a CTA slot (below that,
-    heaviest-first whole blocks already balance and each split only adds a
-    prologue and a merge); then chunk = total KV tiles / (2 * slots), at
-    least `min_chunk`: about two items per slot, so the heaviest causal
-    blocks no longer set the critical path.  Blocks are listed heaviest
-    piece first (the hardware starts CTAs in list order), a split block's
-    pieces consecutively."""
+    """Work items for fmha_fwd_d64_bf16_items.
+
+    The launch gets at most `waves` x `slots` CTAs (slots = resident CTAs
+    per GPU): the smallest piece size `cap` (KV tiles) is found for which
+    cutting every block into ceil(n / cap) near-equal consecutive KV ranges
+    stays within that count.  A block no longer than `cap` stays whole
+    (kv_end = -1, written directly); the pieces of a split block are partial
+    items merged after the launch.  With one wave every CTA slot runs one
+    item, so the launch takes about the longest piece -- cutting blocks to
+    the count of slots, not to a fixed size, avoids a thin extra wave.
+    Blocks are listed by piece size, largest first (the hardware starts CTAs
+    in list order); a split block's pieces stay consecutive, as the merge
+    expects."""
     if not part:
         return []
     n_kv = [max(0, int(round(b[2] - BLOCK_OVERHEAD))) for b in part]
-    total = sum(n_kv)
-    chunk = max(min_chunk, -(-total // (2 * slots)))
-    if max(n_kv) <= max(chunk, total / slots):
-        return [(b[0], b[1], 0, -1) for b in part]
+    target = max(1, int(waves * slots))
+    lo, hi = max(1, min_chunk), max(max(n_kv), 1)
+    while lo < hi:
+        mid = (lo + hi) // 2
+        if sum(-(-n // mid) for n in n_kv if n > 0) <= target:
+            hi = mid
+        else:
+            lo = mid + 1
+    cap = max(lo, min_chunk)
     groups = []
     for b, n in zip(part, n_kv):
-        if n <= chunk:
+        k = -(-n // cap) if n > 0 else 1
+        if k <= 1:
             groups.append((n, [(b[0], b[1], 0, -1)]))
             continue
-        k = -(-n // chunk)
         edges = [n * i // k for i in range(k + 1)]
         groups.append((n / k, [(b[0], b[1], edges[i], edges[i + 1]) for i in range(k)]))
     groups.sort(key=lambda g: -g[0])  # stable: ties keep the head-major order

@@ -45,6 +45,12 @@ def _run(w, dev, mode: str = "entry", world: int = 8):
         blocks = shard.plan_blocks(w.batch, w.heads, w.seqlen, w.seqlen, w.causal, w.varlen_seqs)
         for part in shard.partition(blocks, world):
             tiles = torch.from_numpy(shard.tiles_array(part)).to(dev)
+            if mode == "items":
+                items = torch.from_numpy(shard.items_array(shard.plan_items(part))).to(dev)
+                fm.fmha_fwd(q, k, v, causal=w.causal, layout=w.layout, cu_seqlens_q=cu,
+                            cu_seqlens_k=cu, out=o, lse_out=lse, return_lse=lse is not None,
+                            items=items)
+                continue
             splits = shard.choose_splits(tiles.shape[0]) if mode == "splitkv" else 1
             fm.fmha_fwd(q, k, v, causal=w.causal, layout=w.layout, cu_seqlens_q=cu,
                         cu_seqlens_k=cu, out=o, lse_out=lse, return_lse=lse is not None,
@@ -78,6 +84,12 @@ def test_c5a_splitkv_shards(cuda_device):
     """B1 H2 S40000 causal: each of 8 ranks' LPT shares through uniform
     split-KV (shard.choose_splits), as bench.py --shard --gpus 8."""
     _assert(_run(WORKLOADS["c5a"], cuda_device, mode="splitkv"))
+
+
+def test_c5a_item_shards(cuda_device):
+    """B1 H2 S40000 causal: each of 8 ranks' LPT shares cut into one wave of
+    work items (shard.plan_items), as bench.py --shard --items --gpus 8."""
+    _assert(_run(WORKLOADS["c5a"], cuda_device, mode="items"))
 
 
 def test_c5b_lpt_shards(cuda_device):

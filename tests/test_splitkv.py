@@ -105,16 +105,31 @@ def test_plan_items_covers_every_block_once(B, H, S, causal, world):
         _check_items_cover(part, items)
 
 
-def test_plan_items_bounds_the_largest_item():
+def test_plan_items_fills_one_wave():
+    """c5a, rank 0 of 8: the pieces fit in one wave of CTA slots, no piece
+    is longer than the smallest cap that does, and the largest comes first."""
     blocks = shard.plan_blocks(1, 2, 40000, 40000, True)
     part = shard.partition(blocks, 8)[0]
-    items = shard.plan_items(part)
-    total = sum(max(0, int(round(b[2] - shard.BLOCK_OVERHEAD))) for b in part)
-    chunk = -(-total // (2 * 2 * 148))
-    sizes = [(it[3] - it[2]) for it in items if it[3] >= 0]
-    assert sizes and max(sizes) <= max(4, chunk)
-    # heaviest piece first
-    assert sizes[0] == max(sizes)
+    slots = 2 * 148
+    items = shard.plan_items(part, slots=slots)
+    assert len(items) <= slots
+    n_kv = [max(0, int(round(b[2] - shard.BLOCK_OVERHEAD))) for b in part]
+    sizes = [(it[3] - it[2]) if it[3] >= 0 else n_kv[[(b[0], b[1]) for b in part].index(
+        (it[0], it[1]))] for it in items]
+    cap = max(sizes)
+    # one tile less per piece would need more CTAs than the wave has
+    assert sum(-(-n // (cap - 1)) for n in n_kv if n > 0) > slots
+    assert sizes[0] == cap
+    # two waves: about twice the pieces, each about half as long
+    items2 = shard.plan_items(part, slots=slots, waves=2.0)
+    assert slots < len(items2) <= 2 * slots
+
+
+def test_plan_items_keeps_short_blocks_whole():
+    """A share whose blocks already fit the slots is not split at all."""
+    blocks = shard.plan_blocks(32, 32, 4096, 4096, True)
+    part = shard.partition(blocks, 8)[0]
+    assert all(it[3] == -1 for it in shard.plan_items(part))
 
 
 @pytest.mark.gpu
@@ -122,8 +137,8 @@ def test_plan_items_bounds_the_largest_item():
                                                    (False, 1500, 1000, False),
                                                    (True, 2000, 60, True)])
 def test_items_match_oracle(cuda_device, causal, S, slots, varlen):
-    """Small problems planned for many CTA slots, so that most blocks are
-    split into several partial items (and some stay whole)."""
+    """Small problems planned for four waves of CTA slots, so that most
+    blocks are split into several partial items (and some stay whole)."""
     import torch
 
     from fmha_native_b200.synth import Workload, make_inputs
@@ -137,8 +152,9 @@ def test_items_match_oracle(cuda_device, causal, S, slots, varlen):
     o1, l1 = fm.fmha_fwd(q, k, v, causal=causal, return_lse=True, layout=layout,
                          cu_seqlens_q=cu, cu_seqlens_k=cu)
     blocks = shard.plan_blocks(B, H, S, S, causal, seqs)
-    items = shard.plan_items(blocks, slots=slots)
+    items = shard.plan_items(blocks, slots=slots, waves=4.0)
     assert any(it[3] >= 0 for it in items)
+    assert any(it[3] < 0 for it in items) or slots >= 1000
     it_d = torch.from_numpy(shard.items_array(items)).to(cuda_device)
     o2, l2 = fm.fmha_fwd(q, k, v, causal=causal, return_lse=True, layout=layout,
                          cu_seqlens_q=cu, cu_seqlens_k=cu, items=it_d)
