@@ -60,6 +60,26 @@ def build_library(force: bool = False, verbose: bool = False, extra_flags: list[
     return LIB_PATH
 
 
+TRACE_LIB_PATH = os.path.join(PKG_DIR, "libfmha_b200_trace.so")
+
+
+def build_trace_library(force: bool = False) -> str:
+    """The same kernel source with -DFMHA_TRACE: ``libfmha_b200_trace.so``,
+    which adds the per-role timeline stamps (include/fmha_fwd_trace.h)."""
+    deps = DEPS + [os.path.join(REPO_DIR, "include", "fmha_fwd_trace.h")]
+    if not force and not _stale(TRACE_LIB_PATH, deps):
+        return TRACE_LIB_PATH
+    cmd = [
+        nvcc_path(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-DFMHA_TRACE",
+        "-Xcompiler", "-fPIC", "-shared", "--cudart", "static",
+        "-I", os.path.join(REPO_DIR, "include"),
+        *SOURCES, "-o", TRACE_LIB_PATH + ".tmp",
+    ]
+    subprocess.run(cmd, check=True)
+    os.replace(TRACE_LIB_PATH + ".tmp", TRACE_LIB_PATH)
+    return TRACE_LIB_PATH
+
+
 CLI_SRC = os.path.join(PKG_DIR, "host", "bench_fmha_fwd.cpp")
 CLI_PATH = os.path.join(PKG_DIR, "bench_fmha_fwd")
 
@@ -128,6 +148,7 @@ def build_cpp_tests(force: bool = False) -> str | None:
 if __name__ == "__main__":
     build_library(force="--force" in sys.argv, verbose="-v" in sys.argv)
     build_cli(force="--force" in sys.argv)
+    build_trace_library(force="--force" in sys.argv)
     build_test_lib(force="--force" in sys.argv)
     build_cpp_tests(force="--force" in sys.argv)
     print(LIB_PATH)

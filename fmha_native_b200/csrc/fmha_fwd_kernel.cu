@@ -124,6 +124,39 @@ constexpr int kErrTimeoutLoad = 0x101;
 constexpr int kErrTimeoutMma = 0x102;
 constexpr int kErrTimeoutSoftmax = 0x103;
 
+// Trace builds (-DFMHA_TRACE, libfmha_b200_trace.so): clock64 stamps of the
+// pipeline events of pass 0 for kTraceCtas consecutive CTAs, kTraceSteps KV
+// steps each, kTraceSlots events per step (the slot map is in
+// fmha_native_b200/trace.py).  In the product library the stamps compile
+// to nothing.
+#ifdef FMHA_TRACE
+constexpr int kTraceCtas = 64;
+constexpr int kTraceSteps = 64;
+constexpr int kTraceSlots = 16;
+__device__ int g_trace_cta0 = 0;
+__device__ unsigned long long g_trace[kTraceCtas * kTraceSteps * kTraceSlots];
+__device__ __forceinline__ unsigned smid() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
+// Row of this CTA in the trace buffer (-1: not traced); read once per CTA.
+#define FMHA_TRACE_INIT const int trace_row_ = (int)blockIdx.x - g_trace_cta0
+#define FMHA_TRACE_AT(slot, j, val)                                                    \
+    do {                                                                               \
+        if (trace_row_ >= 0 && trace_row_ < kTraceCtas && (j) >= 0 && (j) < kTraceSteps) \
+            g_trace[(trace_row_ * kTraceSteps + (j)) * kTraceSlots + (slot)] = (val);   \
+    } while (0)
+#else
+#define FMHA_TRACE_INIT \
+    do {                \
+    } while (0)
+#define FMHA_TRACE_AT(slot, j, val) \
+    do {                            \
+    } while (0)
+#endif
+#define FMHA_TRACE_CLOCK(slot, j) FMHA_TRACE_AT(slot, j, clock64())
+
 struct KernelArgs {
     CUtensorMap tm_q;
     CUtensorMap tm_k;
@@ -326,6 +359,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 
     TileWork w;
     if (!decode_work<kCausal, kVarlen>(a, w)) return;  // CTA-uniform early out
+    FMHA_TRACE_INIT;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -357,6 +391,10 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (threadIdx.x == 0) {
+        FMHA_TRACE_CLOCK(7, 0);
+        FMHA_TRACE_AT(7, 1, smid());
+    }
     const uint32_t tmem = sm.tmem_base;
 
     // Per-tile KV counts as scalars (a runtime-indexed array would live in
@@ -417,6 +455,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                                        w.off_k + (w.j0 + (li >> 1)) * kBlockN, w.kvh,
                                        kVarlen ? 0 : w.b, pol_kv);
                 issued = idx + 1;
+                if (pass == 0) FMHA_TRACE_CLOCK(14 + (li & 1), li >> 1);
             }
             }
             if (!ok || *abort_flag) {
@@ -519,25 +558,31 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 if (j + 1 >= n_kv(i)) continue;
                 if (!k_used) {
                     ok = wait_all(&sm.bar_full[slot_of(k_idx)], full_parity(k_idx));
+                    if (leader && G == 0) FMHA_TRACE_CLOCK(8, j);
                     if (!ok) break;
                     k_used = true;
                 }
                 ok = wait_all(&sm.bar_sfree[i], g & 1);
+                if (leader && G == 0) FMHA_TRACE_CLOCK(9, j);
                 if (!ok) break;
                 tc_fence_after();
                 issue_s(i, slot_of(k_idx));
+                if (leader && G == 0) FMHA_TRACE_CLOCK(5, j);
                 commit(&sm.bar_s[i]);
             }
             if (!ok) break;
             if (k_used) commit(&sm.bar_empty[slot_of(k_idx)]);
             ok = wait_all(&sm.bar_full[slot_of(v_idx)], full_parity(v_idx));
+            if (leader && G == 0) FMHA_TRACE_CLOCK(10, j);
             if (!ok) break;
             for (int i = 0; i < kTilesPerCta; ++i) {
                 if (j >= n_kv(i)) continue;
                 ok = wait_all(&sm.bar_p[i], g & 1);
+                if (leader && G == 0) FMHA_TRACE_CLOCK(11, j);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(i, slot_of(v_idx), j > 0);
+                if (leader && G == 0) FMHA_TRACE_CLOCK(6, j);
                 commit(&sm.bar_pv[i]);
                 if (j == n_kv(i) - 1) commit(&sm.bar_o[i]);
             }
@@ -550,6 +595,31 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
         drain_phase(smem_u32(&sm.bar_drain), 0, a);
         __syncwarp();
     }
+#ifdef FMHA_TRACE
+    else if (warp == kWarpMma + 1 && n_max > 0 && trace_row_ >= 0 &&
+             trace_row_ < kTraceCtas) {
+        // Trace builds only: an otherwise idle warp watches the MMA commits
+        // of pass 0 and stamps when S(j) and PV(j) complete.
+        // try_wait parks the warp until the phase completes (or its time
+        // hint runs out), so the observer takes few issue slots.
+        auto seen = [&](uint64_t* bar, uint32_t parity) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(smem_u32(bar), parity)) {
+                if (*abort_flag || globaltimer_ns() - t0 > a.wait_limit_ns) return false;
+            }
+            return true;
+        };
+        if (seen(&sm.bar_s[0], 0) && lane == 0) FMHA_TRACE_CLOCK(12, 0);
+        for (int j = 0; j < n_max; ++j) {
+            if (j + 1 < n_max) {
+                if (!seen(&sm.bar_s[0], (j + 1) & 1)) break;
+                if (lane == 0) FMHA_TRACE_CLOCK(12, j + 1);
+            }
+            if (!seen(&sm.bar_pv[0], j & 1)) break;
+            if (lane == 0) FMHA_TRACE_CLOCK(13, j);
+        }
+    }
+#endif
     } else {
         regs_inc<kRegsSoftmax>();
         // ------------------------------------------------------ softmax groups
@@ -602,6 +672,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 return false;
             }
             tc_fence_after();
+            if (fixed_ref && threadIdx.x == 0) FMHA_TRACE_CLOCK(0, j);
             uint32_t r[4][32];
 #pragma unroll
             for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, r[c]);
@@ -612,6 +683,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             // S_i(j+1) while this group computes P_i(j).
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_sfree[i]));
+            if (fixed_ref && threadIdx.x == 0) FMHA_TRACE_CLOCK(1, j);
 
             const int k0 = (w.j0 + j) * kBlockN;
             const bool need_mask = (k0 + kBlockN > w.seqlen_k) ||
@@ -681,6 +753,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             };
             if (need_mask) exp_tile(std::false_type{});
             else exp_tile(std::true_type{});
+            if (fixed_ref && threadIdx.x == 0) FMHA_TRACE_CLOCK(2, j);
             const float2 s01 = fadd2(fadd2(sum[0], sum[1]), fadd2(sum[2], sum[3]));
             const float tsum = s01.x + s01.y;
             l_run = fmaf(l_run, alpha, tsum);
@@ -697,6 +770,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
                 tc_fence_after();
             }
+            if (fixed_ref && threadIdx.x == 0) FMHA_TRACE_CLOCK(3, j);
             tmem_st32(tP, p[0]);
             tmem_st32(tP + 32, p[1]);
             if (j > 0 && __any_sync(0xffffffffu, upd)) {
@@ -719,6 +793,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&sm.bar_p[i]));
+            if (fixed_ref && threadIdx.x == 0) FMHA_TRACE_CLOCK(4, j);
                     return true;
         };
         if (n > 0 && step(0, std::true_type{})) {
@@ -1404,6 +1479,35 @@ int noalloc_status(cudaStream_t stream) {
 }
 
 }  // namespace
+
+#ifdef FMHA_TRACE
+// Trace-build entry points (include/fmha_fwd_trace.h).
+extern "C" {
+int fmha_fwd_d64_trace_shape(int* ctas, int* steps, int* slots) {
+    if (!ctas || !steps || !slots) return FMHA_ERR_ARG;
+    *ctas = kTraceCtas;
+    *steps = kTraceSteps;
+    *slots = kTraceSlots;
+    return FMHA_OK;
+}
+int fmha_fwd_d64_trace_configure(int first_cta) {
+    if (first_cta < 0) return FMHA_ERR_ARG;
+    void* buf = nullptr;
+    if (cudaMemcpyToSymbol(g_trace_cta0, &first_cta, sizeof(int)) != cudaSuccess ||
+        cudaGetSymbolAddress(&buf, g_trace) != cudaSuccess ||
+        cudaMemset(buf, 0, sizeof(unsigned long long) * kTraceCtas * kTraceSteps * kTraceSlots) !=
+            cudaSuccess)
+        return FMHA_ERR_DEVICE;
+    return FMHA_OK;
+}
+int fmha_fwd_d64_trace_read(unsigned long long* dst, size_t count) {
+    if (!dst || count > (size_t)kTraceCtas * kTraceSteps * kTraceSlots) return FMHA_ERR_ARG;
+    return cudaMemcpyFromSymbol(dst, g_trace, count * sizeof(unsigned long long)) == cudaSuccess
+               ? FMHA_OK
+               : FMHA_ERR_DEVICE;
+}
+}  // extern "C"
+#endif
 
 extern "C" {
 
