@@ -360,6 +360,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
     TileWork w;
     if (!decode_work<kCausal, kVarlen>(a, w)) return;  // CTA-uniform early out
     FMHA_TRACE_INIT;
+    if (threadIdx.x == 0) FMHA_TRACE_CLOCK(7, 7);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -419,6 +420,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 if (n_kv(i) == 0) continue;
                 const uint32_t bar = smem_u32(&sm.bar_q[i]);
                 mbar_arrive_expect_tx(bar, kTileBytes);
+                FMHA_TRACE_CLOCK(7, 5);
                 tma_load_rows<kVarlen>(smem_u32(sm.q[i]), &a.tm_q, bar,
                                        w.off_q + w.row0 + i * kBlockM, w.h, qbatch, pol_q);
             }
@@ -525,6 +527,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 
         for (int i = 0; i < kTilesPerCta && ok; ++i)
             if (n_kv(i) > 0) ok = wait_all(&sm.bar_q[i], 0);
+        if (leader) FMHA_TRACE_CLOCK(7, 6);
         // Pass 0 is the whole schedule; pass 1 (the exact rerun) repeats it
         // when the softmax asks for it, flat step index G + j.
         for (int pass = 0; pass < 2 && ok && n_max > 0; ++pass) {
@@ -825,6 +828,7 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                                   kErrTimeoutSoftmax);
             ok = __all_sync(0xffffffffu, got);
         }
+        if (threadIdx.x == 0) FMHA_TRACE_CLOCK(7, 2);
         if (ok) {
             uint32_t o[2][32];
             if (n > 0) {
@@ -899,11 +903,13 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
                 }
             }
         }
+        if (threadIdx.x == 0) FMHA_TRACE_CLOCK(7, 3);
 }
 
     // ---------------------------------------------------------- teardown
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) FMHA_TRACE_CLOCK(7, 4);
     if (warp == kWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);

@@ -14,7 +14,10 @@ slot  event                                                     role
 4     P(j) in TMEM, p_full arrived                              softmax
 5     S(j+1) MMAs issued                                        MMA warp
 6     PV(j) MMAs issued                                         MMA warp
-7     step 0: CTA start; step 1: SM id                          --
+7     per CTA, by step index: 7 kernel entry, 0 set-up done      --
+      (barriers, TMEM), 1 SM id, 5 Q TMA issued, 6 Q landed
+      (MMA warp), 2 O complete seen, 3 epilogue stores issued,
+      4 CTA past its final barrier
 8     K(j+1) landed (seen by the MMA warp)                      MMA warp
 9     s_free(j) seen                                            MMA warp
 10    V(j) landed                                               MMA warp
@@ -60,6 +63,47 @@ SEGMENTS = [
     ("slack: PV(j-1) complete before softmax needs it", (3, 0), (13, -1)),
     ("TMA: K(j+1) issue -> landed", (8, 0), (14, 1)),
 ]
+
+
+# Per-CTA segments: slot-7 stamps (by step index) and the first/last steps.
+CTA_SEGMENTS = [
+    ("entry -> set-up done (barriers, TMEM alloc)", ("c", 0), ("c", 7)),
+    ("set-up done -> Q TMA issued", ("c", 5), ("c", 0)),
+    ("Q TMA issued -> Q landed (MMA warp)", ("c", 6), ("c", 5)),
+    ("Q landed -> S(0) complete", ("s", 12, 0), ("c", 6)),
+    ("S(0) complete -> seen by softmax", ("s", 0, 0), ("s", 12, 0)),
+    ("first step (row max) s_free(0) -> s_free(1)", ("s", 1, 1), ("s", 1, 0)),
+    ("last p_full -> O complete seen", ("c", 2), ("s", 4, -1)),
+    ("O complete -> epilogue stores issued", ("c", 3), ("c", 2)),
+    ("epilogue -> CTA past its final barrier", ("c", 4), ("c", 3)),
+    ("whole CTA (entry -> final barrier)", ("c", 4), ("c", 7)),
+]
+
+
+def _stamp(T, n, ref):
+    if ref[0] == "c":
+        return T[ref[1], 7]
+    step = ref[2] if ref[2] >= 0 else n + ref[2]
+    return T[step, ref[1]]
+
+
+def summarize_cta(t: np.ndarray) -> Dict[str, object]:
+    """Median per-CTA prologue / epilogue segments (cycles) over the traced
+    CTAs that ran at least two KV steps, and their median step count."""
+    vals: Dict[str, List[float]] = {name: [] for name, _, _ in CTA_SEGMENTS}
+    steps = []
+    for c in range(t.shape[0]):
+        T = t[c]
+        n = int((T[:, 4] > 0).sum())
+        if n < 2 or T[4, 7] == 0:
+            continue
+        steps.append(n)
+        for name, e, b in CTA_SEGMENTS:
+            x, y = _stamp(T, n, e), _stamp(T, n, b)
+            if x > 0 and y > 0:
+                vals[name].append(float(x - y))
+    return {"ctas": len(steps), "steps": statistics.median(steps) if steps else None,
+            "segments": {k: (statistics.median(v) if v else None) for k, v in vals.items()}}
 
 
 def load_trace_library(path: str = TRACE_LIB_PATH) -> ctypes.CDLL:
@@ -152,6 +196,10 @@ def main() -> None:
     print(f"config {args.config}: CTAs {args.first_cta}..{args.first_cta + t.shape[0] - 1}, "
           f"{s['ctas']} traced with >= 6 KV steps; median cycles per KV step")
     for name, v in s["segments"].items():
+        print(f"  {name:52s} {v if v is None else round(v):>8}")
+    c = summarize_cta(t)
+    print(f"per CTA (median over {c['ctas']} CTAs, {c['steps']} KV steps each):")
+    for name, v in c["segments"].items():
         print(f"  {name:52s} {v if v is None else round(v):>8}")
 
 
