@@ -180,29 +180,33 @@ def cpu_sample(w):
                 "b": 1, "h": h, "sq": sq, "sk": s, "causal": w.causal,
                 "flops": 4.0 * h * keys * 64}
     b, h, s = w.batch, w.heads, w.seqlen
+    hk = w.heads_k
     sq = int(min(256, s, max(16, CPU_SAMPLE_MAC / (b * h * s * 64 * 2))))
     flops = 4.0 * b * h * sq * s * 64
     if w.causal:
         # rows i = S-sq..S-1 attend i+1 keys
         keys = sum(range(s - sq + 1, s + 1))
         flops = 4.0 * b * h * keys * 64
-    return {"desc": f"B{b} H{h}: last {sq} query rows x {s} keys ({'causal' if w.causal else 'non-causal'})",
-            "b": b, "h": h, "sq": sq, "sk": s, "causal": w.causal, "flops": flops}
+    kv = f" Hkv{hk}" if hk != h else ""
+    return {"desc": f"B{b} H{h}{kv}: last {sq} query rows x {s} keys "
+                    f"({'causal' if w.causal else 'non-causal'})",
+            "b": b, "h": h, "hk": hk, "sq": sq, "sk": s, "causal": w.causal, "flops": flops}
 
 
 def time_cpu_reference(O, sample, steps, warmup):
     import numpy as np
 
     b, h, sq, sk = sample["b"], sample["h"], sample["sq"], sample["sk"]
+    hk = sample.get("hk", h)
     rng = np.random.default_rng(0)
     q = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sq * 64).astype(np.float32))
-    k = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sk * 64).astype(np.float32))
-    v = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * h * sk * 64).astype(np.float32))
+    k = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * hk * sk * 64).astype(np.float32))
+    v = O.f32_to_bf16_bits_trunc(rng.standard_normal(b * hk * sk * 64).astype(np.float32))
     o = np.zeros(b * h * sq * 64, np.uint16)
     times = []
     for it in range(warmup + steps):
         t0 = time.perf_counter()
-        O.ref_verify(b, h, h, sq, sk, int(sample["causal"]), [], q, k, v, o)
+        O.ref_verify(b, h, hk, sq, sk, int(sample["causal"]), [], q, k, v, o)
         dt = time.perf_counter() - t0
         if it >= warmup:
             times.append(dt)
@@ -398,7 +402,7 @@ def native_arm(args, workload_key):
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": w.name, "per_gpu_batch": w.batch if not args.shard else None,
                        "global_batch": w.batch if args.shard else w.batch * world,
-                       "heads": w.heads, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
+                       "heads": w.heads, "kv_heads": w.heads_k, "seq_len": w.seqlen, "head_dim": 64, "causal": w.causal,
                        "lse": w.lse,
                        "splitkv": (f"per-block: {items.shape[0]} items, "
                                    f"{int((items[:, 3] >= 0).sum().item())} partial"

@@ -26,6 +26,11 @@ class Workload:
     dist: str = "normal"          # "normal" N(0,1) or "uniform" U[-1,1)
     layout: str = "bshd"          # dense "bshd"; varlen "thd"
     varlen_seqs: Optional[Sequence[int]] = None
+    kv_heads: int = 0             # K/V heads (GQA/MQA); 0 = heads
+
+    @property
+    def heads_k(self) -> int:
+        return self.kv_heads or self.heads
 
     def flops(self) -> float:
         """Reference FLOP convention (src/bench_fmha_fwd.cpp:225-226):
@@ -59,6 +64,14 @@ WORKLOADS = {
     "c5b": Workload("B32 H32 S4096 D64 bf16 causal", 32, 32, 4096, True, False),
     # one eighth of c5b (its per-rank share at 8 GPUs): the profiling case
     "c5b_s8": Workload("B4 H32 S4096 D64 bf16 causal (c5b / 8)", 4, 32, 4096, True, False),
+    # c5b's shape with grouped K/V: 4 query heads per K/V head, and one K/V head
+    # for all 32 (the reference's GQA/MQA test ratios, tests/test_configs.hpp:27-31,66-67)
+    "c5b_gqa4": Workload("B32 H32 Hkv8 S4096 D64 bf16 causal (GQA 4)", 32, 32, 4096, True,
+                         False, kv_heads=8),
+    "c5b_mqa": Workload("B32 H32 Hkv1 S4096 D64 bf16 causal (MQA)", 32, 32, 4096, True, False,
+                        kv_heads=1),
+    "c2_gqa4": Workload("B4 H16 Hkv4 S2048 D64 bf16 non-causal (GQA 4)", 4, 16, 2048, False,
+                        False, kv_heads=4),
 }
 
 
@@ -81,12 +94,14 @@ def make_inputs(w: Workload, device, seed_base: int = 0):
     if w.varlen_seqs:
         total = w.tokens()
         shape = (total, w.heads, 64)
+        shape_kv = (total, w.heads_k, 64)
         cu = torch.tensor(np.concatenate([[0], np.cumsum(w.varlen_seqs)]).astype(np.int32),
                           device=device)
     else:
         shape = (w.batch, w.seqlen, w.heads, 64)
+        shape_kv = (w.batch, w.seqlen, w.heads_k, 64)
         cu = None
     q = make_tensor(shape, seed_base + 0, w.dist, device)
-    k = make_tensor(shape, seed_base + 1, w.dist, device)
-    v = make_tensor(shape, seed_base + 2, w.dist, device)
+    k = make_tensor(shape_kv, seed_base + 1, w.dist, device)
+    v = make_tensor(shape_kv, seed_base + 2, w.dist, device)
     return q, k, v, cu

@@ -80,6 +80,13 @@ def test_baseline_config_entry(cuda_device, key):
     _assert(_run(WORKLOADS[key], cuda_device))
 
 
+@pytest.mark.parametrize("key", ["c5b_gqa4", "c5b_mqa", "c2_gqa4"])
+def test_grouped_kv_config_entry(cuda_device, key):
+    """c5b / c2 shapes with 4 query heads per K/V head and with one K/V head
+    (the reference's GQA/MQA ratios), full size, against the device oracle."""
+    _assert(_run(WORKLOADS[key], cuda_device))
+
+
 def test_c5a_splitkv_shards(cuda_device):
     """B1 H2 S40000 causal: each of 8 ranks' LPT shares through uniform
     split-KV (shard.choose_splits), as bench.py --shard --gpus 8."""
