@@ -166,6 +166,7 @@ struct KernelArgs {
     const int32_t* seqstart_q;
     const int32_t* seqstart_k;
     const int32_t* seq_order;  // varlen launch order: slot -> sequence, longest first (or null)
+    const int2* block_map;     // compact varlen launch: CTA / nhead_q -> (sequence, query block)
     long long stride_o, nhead_stride_o, batch_stride_o;
     int seqlen_q, seqlen_k;
     int nhead_q, nhead_k;
@@ -260,6 +261,13 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
         if (a.num_splits > 1) split = (int)blockIdx.x % a.num_splits;
         hb = a.tiles[2 * x];
         mblk = a.tiles[2 * x + 1];
+    } else if (kVarlen && a.block_map != nullptr) {
+        // Compact varlen launch: nhead_q consecutive CTAs per query block,
+        // blocks in the order of the map (longest sequence first).
+        const int2 e = a.block_map[(int)blockIdx.x / a.nhead_q];
+        if (e.x < 0) return false;  // past the last block
+        hb = e.x * a.nhead_q + (int)blockIdx.x % a.nhead_q;
+        mblk = e.y;
     } else {
         // Launch order: (batch, head) pairs in groups of head_group whose K/V
         // fit in L2 together; inside a group causal blocks go heaviest first
@@ -282,7 +290,8 @@ __device__ __forceinline__ bool decode_work(const KernelArgs& a, TileWork& w) {
     w.kvh = w.h / (a.nhead_q / a.nhead_k);
     if constexpr (kVarlen) {
         // Full varlen launch: batch slots are walked longest sequence first.
-        if (a.seq_order != nullptr && a.tiles == nullptr && a.items == nullptr)
+        if (a.seq_order != nullptr && a.block_map == nullptr && a.tiles == nullptr &&
+            a.items == nullptr)
             w.b = a.seq_order[w.b];
         w.off_q = a.seqstart_q[w.b];
         w.off_k = a.seqstart_k[w.b];
@@ -924,8 +933,10 @@ fmha_fwd_d64_sm100_kernel(const __grid_constant__ KernelArgs a) {
 // block index within a sequence).  One CTA; rank by counting.
 __global__ void __launch_bounds__(1024)
 fmha_fwd_d64_varlen_order(const int32_t* __restrict__ seqstart, int batch,
-                          int32_t* __restrict__ order) {
+                          int32_t* __restrict__ order, int2* __restrict__ block_map,
+                          int map_cap, int causal) {
     extern __shared__ int32_t lens[];
+    __shared__ int warp_tot[32];
     for (int b = threadIdx.x; b < batch; b += blockDim.x) lens[b] = seqstart[b + 1] - seqstart[b];
     __syncthreads();
     for (int b = threadIdx.x; b < batch; b += blockDim.x) {
@@ -937,6 +948,50 @@ fmha_fwd_d64_varlen_order(const int32_t* __restrict__ seqstart, int batch,
         }
         order[rank] = b;
     }
+    if (block_map == nullptr) return;
+    __syncthreads();
+    // Block map of the compact launch: position p of the rank-ordered list
+    // of query blocks (longest sequence first; inside a sequence the
+    // heaviest block first when causal) -> (sequence, query block).  Each
+    // thread owns a contiguous run of ranks; an exclusive scan over the
+    // threads' block counts gives where its run starts.
+    const int seg = (batch + blockDim.x - 1) / blockDim.x;
+    const int r0 = min(batch, (int)threadIdx.x * seg), r1 = min(batch, r0 + seg);
+    auto nblk = [&](int r) { return (max(lens[order[r]], 0) + kBlockM - 1) / kBlockM; };
+    int mine = 0;
+    for (int r = r0; r < r1; ++r) mine += nblk(r);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int incl = mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_tot[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+        const int nw = (blockDim.x + 31) >> 5;
+        int t = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, t, d);
+            if (lane >= d) t += v;
+        }
+        warp_tot[lane] = t;  // inclusive over warps
+    }
+    __syncthreads();
+    int pos = incl - mine + (wid > 0 ? warp_tot[wid - 1] : 0);
+    for (int r = r0; r < r1; ++r) {
+        const int b = order[r];
+        const int nb = nblk(r);
+        for (int mi = 0; mi < nb && pos < map_cap; ++mi, ++pos)
+            block_map[pos] = make_int2(b, causal ? nb - 1 - mi : mi);
+    }
+    // Positions past the last block (the grid is sized by an upper bound)
+    // are marked empty.
+    const int total = warp_tot[((blockDim.x + 31) >> 5) - 1];
+    for (int q = total + (int)threadIdx.x; q < map_cap; q += blockDim.x)
+        block_map[q] = make_int2(-1, -1);
 }
 
 // Split-KV merge: partial slots [slot0, slot0 + nparts) of query block mblk
@@ -1329,7 +1384,17 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
         n_work = n_items;
     }
     if (varlen && tiles == nullptr && items == nullptr && batch > 1 && batch <= kOrderMaxBatch) {
-        int32_t* order = nullptr;
+        // Compact launch: nhead_q CTAs per real query block (a sequence of
+        // length L has ceil(L/128) blocks, at most total_q/128 + batch in
+        // all), in the order of a block map built on the device, instead of
+        // max-blocks x batch x heads CTAs of which the short sequences' tail
+        // would exit at once.
+        const long long cap_ll = std::min<long long>((long long)a.m_blocks * batch,
+                                                     (long long)total_q / kBlockM + batch);
+        const int cap = (int)cap_ll;
+        const size_t order_ints = ((size_t)batch + 1) & ~(size_t)1;  // keeps the map 8-byte aligned
+        const size_t need = order_ints + 2 * (size_t)cap;             // in int32 units
+        int32_t* buf = nullptr;
         {
             std::lock_guard<std::mutex> lock(g_mutex);
             std::pair<int32_t*, int>* slot = nullptr;
@@ -1339,19 +1404,22 @@ int launch(const FmhaFwdParams* p, int batch, bool causal, bool varlen, int tota
                 ctx->orders.push_back({stream, {nullptr, 0}});
                 slot = &ctx->orders.back().second;
             }
-            if (slot->second < batch) {
+            if ((size_t)slot->second < need) {
                 if (slot->first) cudaFree(slot->first);
                 slot->first = nullptr;
                 slot->second = 0;
-                if (cudaMalloc(&slot->first, sizeof(int32_t) * (size_t)batch) != cudaSuccess)
+                if (cudaMalloc(&slot->first, sizeof(int32_t) * need) != cudaSuccess)
                     return FMHA_ERR_LAUNCH;
-                slot->second = batch;
+                slot->second = (int)need;
             }
-            order = slot->first;
+            buf = slot->first;
         }
+        int2* map = reinterpret_cast<int2*>(buf + order_ints);
         fmha_fwd_d64_varlen_order<<<1, 1024, sizeof(int32_t) * (size_t)batch, stream>>>(
-            p->seqstart_q, batch, order);
-        a.seq_order = order;
+            p->seqstart_q, batch, buf, map, cap, causal ? 1 : 0);
+        a.seq_order = buf;
+        a.block_map = map;
+        n_work = cap * p->nhead_q;
     }
     if ((st = launch_main(a, causal, varlen, n_work, stream)) != FMHA_OK)
         return st;
