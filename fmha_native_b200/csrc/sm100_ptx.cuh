@@ -82,7 +82,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 // 4-D tiled bulk tensor load global -> shared, completion via mbarrier tx
-// bytes.  No multicast.  `policy` is an L2 cache-policy descriptor.
+// bytes (this CTA only).  `policy` is an L2 cache-policy descriptor.
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar,
                                             int c0, int c1, int c2, int c3, uint64_t policy) {
     asm volatile(
